@@ -1,0 +1,103 @@
+/*
+ * qf_b200.h -- C ABI of the B200 (sm_100a) W8A16 decode-GEMM library (libqf_b200.so).
+ *
+ * The library replaces the Triton kernel behind EurekaZang/qwen-a100-fastpath's vLLM plugin
+ * (plugin/qwen_fastpath/w8a16.py) for the QWEN_FAST_LINEAR linear method and the QWEN_FAST_DRAFT_HEAD
+ * int8 draft LM head.  Signatures carry plain pointers, sizes and a CUDA stream handle only; no
+ * framework types.  All pointers are device pointers owned by the caller (borrowed for the call); every
+ * entry point enqueues on `stream` and returns without synchronising, so calls can be captured into a
+ * CUDA graph once the workspace exists.
+ *
+ * Layouts (the tensors vLLM already holds; no repacking, no second weight copy):
+ *   x      bf16 [M, K], row stride ldx elements, unit column stride           (activations, M <= 16)
+ *   w      int8 [N, K] row-major, row stride ldw bytes == vLLM's w_q [K, N] view with stride (1, ldw)
+ *   scale  fp32 [N], per output channel (vLLM's w_s [N, 1] read flat)
+ *   y      [M, N] row stride ldy elements, bf16 or fp32
+ *
+ * Math (matches w8a16.py:15-44): y[m,n] = round_out( scale[n] * sum_k x[m,k] * (float)w[n,k] ) with exact
+ * bf16 x int8 products accumulated in fp32; with bias, round_bf16( (float)y_bf16 + (float)bias[n] ) as the
+ * reference's separate `y + bias` (patches.py:96-97).
+ *
+ * Alignment: x, w 16-byte aligned; ldx % 8 == 0 (bf16 elements); ldw % 16 == 0 (bytes).  These are the
+ * TMA tensor-map rules; a caller with other strides makes the rows contiguous first.
+ *
+ * Workspace: `ws` (>= qf_w8a16_workspace_bytes()) must be zero-filled once when allocated; every call
+ * leaves its counters at zero again.  Calls that share a workspace must be ordered on one stream.  The
+ * first word of the workspace is a sticky device error flag (see qf_workspace_status).
+ *
+ * Return values: QF_OK (0) or a negative QF_ERR_* code; qf_last_error_detail() gives a message
+ * (thread-local).
+ */
+#ifndef QF_B200_H
+#define QF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QF_ABI_VERSION 1
+
+#define QF_OK 0
+#define QF_ERR_INVALID (-1)   /* null pointer or bad argument */
+#define QF_ERR_SHAPE (-2)     /* M, N, K or n_valid out of range */
+#define QF_ERR_STRIDE (-3)    /* leading dimension smaller than the row */
+#define QF_ERR_ALIGN (-4)     /* pointer or stride alignment not met */
+#define QF_ERR_ARCH (-5)      /* current device is not compute capability 10.0 (B200 / sm_100a) */
+#define QF_ERR_WORKSPACE (-6) /* workspace missing or too small */
+#define QF_ERR_LAUNCH (-7)    /* CUDA runtime error at launch */
+#define QF_ERR_DTYPE (-8)     /* unsupported output dtype */
+#define QF_ERR_TIMEOUT (-9)   /* a bounded device-side wait expired (reported through the workspace) */
+#define QF_ERR_DRIVER (-10)   /* driver entry point cuTensorMapEncodeTiled unavailable / rejected */
+
+#define QF_DTYPE_BF16 0
+#define QF_DTYPE_F32 1
+
+#define QF_MAX_M 16        /* rows per call (the reference's SMALL_M, w8a16.py:12) */
+#define QF_MAX_N 1048576   /* output channels per call (tile-counter capacity of the workspace) */
+
+/* flags */
+#define QF_FLAG_PDL 1u     /* launch with programmatic dependent launch: the weight prefetch of this call may
+                              overlap the previous kernel on the stream (weights and scales must not be written
+                              by that kernel; activations, outputs and workspace are only touched after it
+                              completes) */
+
+/* Bytes of workspace a call with these sizes needs (fixed prefix of counters + split-K partials + head
+ * statistics).  No CUDA call is made. */
+size_t qf_w8a16_workspace_bytes(int M, int N, int K);
+
+/* Small-M W8A16 GEMM.  Replaces `w8a16_mm(x, w_t, w_scale, cfg, out_dtype)` (plugin/qwen_fastpath/w8a16.py:71-83)
+ * plus the fused bias of `qf_int8_linear` (plugin/qwen_fastpath/patches.py:84-98).  bias: bf16 [N] or NULL.
+ * y_dtype: QF_DTYPE_BF16 or QF_DTYPE_F32 (fp32 exports the pre-rounding accumulator * scale; bias is then
+ * added in fp32).  1 <= M <= 16; M == 0 or N == 0 is a no-op; K == 0 writes zeros (+ bias). */
+int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
+                  const void* bias, void* y, int64_t ldy, int y_dtype, int M, int N, int K,
+                  void* ws, size_t ws_bytes, unsigned flags, void* stream);
+
+/* Int8 draft LM head with fused per-row statistics.  Replaces `int8_logits` + `compute_logits` +
+ * `get_top_tokens` (plugin/qwen_fastpath/patches.py:157-185): bf16 logits [M, N] (ldl; NULL skips the
+ * store), and over columns [0, n_valid) of the same bf16 logits: row_max (fp32), row_argmax (int64, first
+ * index on ties, + vocab_offset) and row_lse (fp32 logsumexp).  Columns >= n_valid are the vocab padding
+ * the reference masks to -inf (patches.py:182-184).  1 <= n_valid <= N; 1 <= M <= 16; K >= 1. */
+int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
+                  void* logits, int64_t ldl, int M, int N, int K, int n_valid, int64_t vocab_offset,
+                  float* row_max, int64_t* row_argmax, float* row_lse,
+                  void* ws, size_t ws_bytes, unsigned flags, void* stream);
+
+/* Reads and clears the workspace's sticky device error flag (synchronises `stream`).  *status receives
+ * QF_OK or QF_ERR_TIMEOUT.  Not for the hot path. */
+int qf_workspace_status(void* ws, void* stream, int* status);
+
+/* Static description of the error code. */
+const char* qf_strerror(int code);
+/* Message of the last failing call on this thread. */
+const char* qf_last_error_detail(void);
+/* QF_ABI_VERSION of the built library. */
+int qf_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QF_B200_H */

@@ -1,0 +1,234 @@
+"""CPU oracle for the W8A16 decode-GEMM path (test infrastructure only).
+
+This module is the checker, never the product: only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it.  The CUDA library in
+``qwen_a100_fastpath_b200`` never calls into it and fails loudly when its extension is missing.
+
+It restates, in numpy, the arithmetic of EurekaZang/qwen-a100-fastpath's ``qwen_fastpath`` plugin:
+
+* ``dequant_matmul_f32``  -- the reference's exact-product oracle
+  ``F.linear(x.float(), W.float() * ws[:, None])`` chunked over 8192 output rows
+  (bench/test_w8a16.py:15; same expression in bench/kernels/linear_kernels.py:91).
+* ``w8a16_mm``            -- the kernel's contract (plugin/qwen_fastpath/w8a16.py:15-44, :71-83):
+  ``y[m, n] = s[n] * sum_k x[m, k] * W[n, k]`` with exact bf16 x int8 products, fp32 accumulation,
+  the per-channel scale applied to the accumulator, then one round to the output dtype.
+* ``qf_int8_linear``      -- the op wrapper (plugin/qwen_fastpath/patches.py:84-101): leading dims
+  flattened, bias added *after* the bf16 round as a separate bf16 op (two roundings).
+* ``quantize_rows``       -- the draft lm_head int8 quantizer (plugin/qwen_fastpath/patches.py:143-147).
+* ``top_tokens`` / ``head_stats`` -- ``get_top_tokens`` (patches.py:182-185: padding columns to -inf,
+  first-index argmax, + vocab start offset) and the fused per-row (max, argmax, logsumexp) over the
+  same bf16 logits.
+
+Parity is pinned: ``tests/golden/make_fixtures.py`` ran the reference's own ``w8a16_mm``,
+``qf_int8_linear`` and draft-head patches (Triton interpreter, with two interpreter bf16 bugs fixed) and
+stored their outputs; ``tests/test_oracle_golden.py`` checks this module against them.
+
+bf16 tensors are carried as ``uint16`` bit patterns (numpy has no bfloat16).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+CHUNK_ROWS = 8192  # bench/test_w8a16.py:15 chunks the fp32 weight copy over 8192 output rows
+
+
+# ----------------------------------------------------------------------------------------------
+# bf16 helpers (round-to-nearest-even, as torch's float -> bfloat16 conversion)
+# ----------------------------------------------------------------------------------------------
+def f32_to_bf16(a) -> np.ndarray:
+    """fp32 -> bf16 bits (uint16), round to nearest, ties to even; NaN stays NaN."""
+    a = np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+    u = a.view(np.uint32).astype(np.uint64)
+    rounded = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(a)
+    if nan.any():
+        rounded = rounded.copy()
+        rounded[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return rounded
+
+
+def bf16_to_f32(b) -> np.ndarray:
+    """bf16 bits (uint16) -> exact fp32 values."""
+    b = np.ascontiguousarray(np.asarray(b, dtype=np.uint16))
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+# ----------------------------------------------------------------------------------------------
+# seeded inputs with the distributions the reference benchmarks on
+# ----------------------------------------------------------------------------------------------
+def make_inputs(seed: int, M: int, N: int, K: int, *, scale_lo: float = 1e-3, scale_hi: float = 1e-2,
+                x_row_stride: int | None = None):
+    """Seeded (x_bf16_bits [M, ldx], W int8 [N, K], scale fp32 [N]).
+
+    W ~ uniform int in [-127, 127] (bench/test_w8a16.py:10), per-output-channel scale ~ U(scale_lo,
+    scale_hi) (bench/test_w8a16.py:11 uses U(1e-3, 1.1e-2); the benchmark configuration uses
+    U(1e-3, 1e-2)), x ~ N(0, 1) rounded to bf16 (bench/test_w8a16.py:13).  ``x_row_stride`` > K pads each
+    activation row (the reference accepts any row stride, plugin/qwen_fastpath/w8a16.py:72); the pad is
+    filled with NaN so that reading it would poison the result.  ``np.random.RandomState`` is used
+    because its streams are frozen across numpy versions.
+    """
+    rs = np.random.RandomState(seed)
+    W = rs.randint(-127, 128, size=(N, K)).astype(np.int8)
+    s = (rs.random_sample(N) * (scale_hi - scale_lo) + scale_lo).astype(np.float32)
+    x = f32_to_bf16(rs.standard_normal((M, K)).astype(np.float32))
+    ldx = K if x_row_stride is None else int(x_row_stride)
+    if ldx != K:
+        xp = np.full((M, ldx), 0x7FC0, dtype=np.uint16)  # bf16 NaN in the pad
+        xp[:, :K] = x
+        x = xp
+    return x, W, s
+
+
+def make_bias(seed: int, N: int) -> np.ndarray:
+    rs = np.random.RandomState(seed)
+    return f32_to_bf16(rs.standard_normal(N).astype(np.float32) * 0.5)
+
+
+# ----------------------------------------------------------------------------------------------
+# the contraction
+# ----------------------------------------------------------------------------------------------
+def dequant_matmul_f32(x_bits, W, s, K: int | None = None) -> np.ndarray:
+    """``F.linear(x.float(), W.float() * ws[:, None])`` chunked over 8192 rows (bench/test_w8a16.py:15).
+
+    fp32 arithmetic throughout, as the reference's oracle.  Returns fp32 [M, N].
+    """
+    K = W.shape[1] if K is None else K
+    x = bf16_to_f32(np.asarray(x_bits)[:, :K])
+    out = []
+    for i in range(0, W.shape[0], CHUNK_ROWS):
+        wd = W[i:i + CHUNK_ROWS].astype(np.float32) * s[i:i + CHUNK_ROWS, None]
+        out.append(x @ wd.T)
+    return np.concatenate(out, axis=1).astype(np.float32) if out else np.zeros((x.shape[0], 0), np.float32)
+
+
+def dequant_matmul_f64(x_bits, W, s, K: int | None = None) -> np.ndarray:
+    """Exact-product reference in fp64: ``s[n] * sum_k x[m,k] W[n,k]`` (the kernel's math, w8a16.py:28-38)."""
+    K = W.shape[1] if K is None else K
+    x = bf16_to_f32(np.asarray(x_bits)[:, :K]).astype(np.float64)
+    out = []
+    for i in range(0, W.shape[0], CHUNK_ROWS):
+        acc = x @ W[i:i + CHUNK_ROWS].astype(np.float64).T
+        out.append(acc * s[i:i + CHUNK_ROWS].astype(np.float64)[None, :])
+    return np.concatenate(out, axis=1) if out else np.zeros((x.shape[0], 0), np.float64)
+
+
+def w8a16_mm(x_bits, W, s, out_dtype: str = "bf16", K: int | None = None) -> np.ndarray:
+    """The kernel contract of ``w8a16_mm`` (plugin/qwen_fastpath/w8a16.py:71-83).
+
+    fp32 accumulator (computed here in fp64, then rounded to fp32 -- the closest fp32 a summation can
+    give), scale applied to the accumulator (w8a16.py:37-38), one rounding to ``out_dtype``.
+    Returns bf16 bits (uint16) or fp32.
+    """
+    y = dequant_matmul_f64(x_bits, W, s, K).astype(np.float32)
+    if out_dtype == "bf16":
+        return f32_to_bf16(y)
+    if out_dtype == "f32":
+        return y
+    raise ValueError(out_dtype)
+
+
+def add_bias_bf16(y_bits, bias_bits) -> np.ndarray:
+    """``y + bias`` on bf16 tensors (plugin/qwen_fastpath/patches.py:96-97): fp32 add, one bf16 round."""
+    return f32_to_bf16(bf16_to_f32(y_bits) + bf16_to_f32(bias_bits)[None, :])
+
+
+def qf_int8_linear(x_bits, W, s, bias_bits=None) -> np.ndarray:
+    """``qf_int8_linear`` small-M branch (plugin/qwen_fastpath/patches.py:84-98) on a [..., K] input.
+
+    ``x_bits`` may carry leading dims; returns bf16 bits [..., N].
+    """
+    x_bits = np.asarray(x_bits)
+    lead = x_bits.shape[:-1]
+    x2 = x_bits.reshape(-1, x_bits.shape[-1])
+    y = w8a16_mm(x2, W, s, "bf16")
+    if bias_bits is not None:
+        y = add_bias_bf16(y, bias_bits)
+    return y.reshape(*lead, W.shape[0])
+
+
+# ----------------------------------------------------------------------------------------------
+# draft LM head
+# ----------------------------------------------------------------------------------------------
+def quantize_rows(weight_bits, block_rows: int = 16384):
+    """Per-row symmetric int8 quantizer of the draft lm_head (plugin/qwen_fastpath/patches.py:143-147).
+
+    ``s = max(|w|, 1e-8) / 127`` in fp32, ``q = clamp(round_half_even(w / s), -127, 127)``.
+    Returns (int8 [V, H], fp32 [V]).
+    """
+    w = bf16_to_f32(weight_bits)
+    V = w.shape[0]
+    q = np.empty(w.shape, dtype=np.int8)
+    sc = np.empty((V,), dtype=np.float32)
+    for i in range(0, V, block_rows):
+        blk = w[i:i + block_rows]
+        s = np.maximum(np.abs(blk).max(axis=1), np.float32(1e-8)).astype(np.float32) / np.float32(127.0)
+        s = s.astype(np.float32)
+        q[i:i + block_rows] = np.clip(np.rint(blk / s[:, None]), -127, 127).astype(np.int8)
+        sc[i:i + block_rows] = s
+    return q, sc
+
+
+def top_tokens(logits_bits, num_pad: int, vocab_start: int = 0) -> np.ndarray:
+    """``get_top_tokens`` (plugin/qwen_fastpath/patches.py:182-185) on bf16 logits [M, V]."""
+    v = bf16_to_f32(logits_bits).astype(np.float64)
+    if num_pad > 0:
+        v[..., -num_pad:] = -np.inf
+    return np.argmax(v, axis=-1).astype(np.int64) + int(vocab_start)
+
+
+def head_stats(logits_bits, n_valid: int, vocab_offset: int = 0):
+    """Per-row (max, argmax, logsumexp) over the first ``n_valid`` bf16 logits of each row.
+
+    max/argmax follow ``torch.argmax`` on the bf16 tensor (first index on ties), with columns
+    ``>= n_valid`` masked as ``get_top_tokens`` masks vocab padding (patches.py:182-184); argmax gets
+    ``vocab_offset`` added (patches.py:185).  logsumexp (the normaliser probabilistic drafting needs) is
+    computed in fp64 over the same bf16 values.  Returns (fp32 [M], int64 [M], fp64 [M]).
+    """
+    v = bf16_to_f32(logits_bits)[:, :n_valid].astype(np.float64)
+    mx = v.max(axis=1)
+    am = np.argmax(v, axis=1).astype(np.int64) + int(vocab_offset)
+    lse = mx + np.log(np.exp(v - mx[:, None]).sum(axis=1))
+    return mx.astype(np.float32), am, lse
+
+
+def top2_gap(logits_bits, n_valid: int) -> np.ndarray:
+    """Gap between the largest and second-largest bf16 logit per row (0 means a tie in bf16)."""
+    v = np.sort(bf16_to_f32(logits_bits)[:, :n_valid].astype(np.float64), axis=1)
+    return v[:, -1] - v[:, -2]
+
+
+# ----------------------------------------------------------------------------------------------
+# tensor-parallel restatement (the reference runs TP=1 only; vLLM's row-parallel linear sums the
+# per-rank partial outputs, model_executor/layers/linear.py:1556-1559 in the vLLM host)
+# ----------------------------------------------------------------------------------------------
+def shard_columns(W, s, rank: int, world: int):
+    """Column-parallel shard: output rows [rank*N/t, (rank+1)*N/t)."""
+    N = W.shape[0]
+    assert N % world == 0
+    n = N // world
+    return W[rank * n:(rank + 1) * n], s[rank * n:(rank + 1) * n]
+
+
+def shard_rows(W, x_bits, rank: int, world: int):
+    """Row-parallel shard: input columns [rank*K/t, (rank+1)*K/t) of W and of x."""
+    K = W.shape[1]
+    assert K % world == 0
+    k = K // world
+    return W[:, rank * k:(rank + 1) * k], np.ascontiguousarray(np.asarray(x_bits)[:, rank * k:(rank + 1) * k])
+
+
+def combine_head_stats(parts):
+    """Merge per-shard (max, argmax, lse) of a vocab-sharded head, in rank order.
+
+    Global max/argmax: largest max, lowest global index on ties.  lse = m* + log(sum_r exp(lse_r - m*)).
+    ``parts`` is a list of (max [M], argmax [M] (global indices), lse [M]).
+    """
+    mx = np.stack([np.asarray(p[0], np.float64) for p in parts])
+    am = np.stack([np.asarray(p[1], np.int64) for p in parts])
+    ls = np.stack([np.asarray(p[2], np.float64) for p in parts])
+    best = mx.max(axis=0)
+    cand = np.where(mx == best[None, :], am, np.iinfo(np.int64).max)
+    arg = cand.min(axis=0)
+    m_star = ls.max(axis=0)
+    lse = m_star + np.log(np.exp(ls - m_star[None, :]).sum(axis=0))
+    return best.astype(np.float32), arg, lse

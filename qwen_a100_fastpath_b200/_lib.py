@@ -1,0 +1,68 @@
+"""ctypes binding of ``libqf_b200.so`` (declarations in include/qf_b200.h).
+
+The library is the only compute path: if it is missing or fails to load, importing this module raises, and
+nothing falls back to a CPU or framework implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libqf_b200.so"
+
+QF_OK = 0
+QF_ERR_TIMEOUT = -9
+QF_DTYPE_BF16 = 0
+QF_DTYPE_F32 = 1
+QF_MAX_M = 16
+QF_MAX_N = 1048576
+QF_FLAG_PDL = 1
+ABI_VERSION = 1
+
+# (name, restype, argtypes) -- one entry per function declared in include/qf_b200.h
+_c = ctypes
+SIGNATURES = [
+    ("qf_w8a16_workspace_bytes", _c.c_size_t, [_c.c_int, _c.c_int, _c.c_int]),
+    ("qf_w8a16_gemm", _c.c_int,
+     [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64,
+      _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_size_t, _c.c_uint, _c.c_void_p]),
+    ("qf_w8a16_head", _c.c_int,
+     [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int,
+      _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+      _c.c_size_t, _c.c_uint, _c.c_void_p]),
+    ("qf_workspace_status", _c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(_c.c_int)]),
+    ("qf_strerror", _c.c_char_p, [_c.c_int]),
+    ("qf_last_error_detail", _c.c_char_p, []),
+    ("qf_abi_version", _c.c_int, []),
+]
+
+
+class QFError(RuntimeError):
+    """A libqf_b200 entry point returned a QF_ERR_* code."""
+
+    def __init__(self, fn: str, code: int):
+        self.code = code
+        detail = LIB.qf_last_error_detail().decode(errors="replace")
+        super().__init__(f"{fn}: {LIB.qf_strerror(code).decode()} ({code}): {detail}")
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH.name} is not built; run `python -m qwen_a100_fastpath_b200.build` "
+                          "(nvcc, sm_100a)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, res, args in SIGNATURES:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.qf_abi_version() != ABI_VERSION:
+        raise ImportError(f"{LIB_PATH.name} ABI {lib.qf_abi_version()} != expected {ABI_VERSION}; rebuild it")
+    return lib
+
+
+LIB = _load()
+
+
+def check(fn: str, code: int) -> None:
+    if code != QF_OK:
+        raise QFError(fn, code)

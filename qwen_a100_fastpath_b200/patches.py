@@ -1,0 +1,202 @@
+"""vLLM patches of the B200 W8A16 decode path (the drop-in boundary).
+
+Same patch targets, guards and fallbacks as ``qwen_fastpath.patches`` of EurekaZang/qwen-a100-fastpath
+(plugin/qwen_fastpath/patches.py:72-189); the kernels behind them are ``libqf_b200.so``:
+
+* ``patch_int8_linear``: ``CutlassInt8ScaledMMLinearKernel.apply_weights(self, layer, x, bias=None)`` routes
+  dynamic symmetric per-token W8A8 linears (patches.py:110) to the opaque custom op
+  ``torch.ops.vllm.qf_int8_linear(x, w_q, w_s, bias)`` (patches.py:84-106).  ``M <= 16`` bf16 rows on a
+  K-major weight with per-channel scales take the B200 kernel (bias fused, rounded like the reference's
+  ``y + bias``); everything else keeps vLLM's CUTLASS W8A8 path (patches.py:99-101).
+* ``patch_draft_lm_head``: an int8 per-row copy of the MTP draft lm_head made at load time
+  (patches.py:133-152), ``compute_logits`` through the int8 head (patches.py:157-174), and ``get_top_tokens``
+  taken from the head kernel's fused argmax (patches.py:176-185), which also yields the per-row logsumexp
+  probabilistic drafting needs (left on the model as ``_qf_head_stats``).
+
+vLLM is imported lazily inside the patch functions; hooks missing from the installed vLLM are skipped with a
+log line instead of failing ``register()``.
+"""
+from __future__ import annotations
+
+import logging
+
+import torch
+
+logger = logging.getLogger("vllm.qwen_fastpath")
+
+
+# ----------------------------------------------------------------------------------------------
+# QWEN_FAST_LINEAR
+# ----------------------------------------------------------------------------------------------
+def make_int8_linear_op():
+    """The ``qf_int8_linear`` implementation and its fake (shape-only) counterpart."""
+    from .w8a16 import SMALL_M, pick_config, w8a16_mm, weight_supported
+
+    def qf_int8_linear(x: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor,
+                       bias: torch.Tensor | None) -> torch.Tensor:
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        M, K = x2.shape
+        N = w_q.shape[1]
+        if (M <= SMALL_M and x2.dtype == torch.bfloat16 and w_q.stride(0) == 1 and w_s.numel() == N
+                and weight_supported(w_q)):
+            cfg = pick_config(N, K)
+            if cfg is not None:
+                y = w8a16_mm(x2, w_q, w_s, cfg, x.dtype, bias=bias, pdl=True)
+                return y.view(*lead, N)
+        from vllm import _custom_ops as ops
+        x_q, x_s, _ = ops.scaled_int8_quant(x2.contiguous(), None, None, symmetric=True)
+        y = ops.cutlass_scaled_mm(x_q, w_q, scale_a=x_s, scale_b=w_s, out_dtype=x.dtype, bias=bias)
+        return y.view(*lead, N)
+
+    def qf_int8_linear_fake(x: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor,
+                            bias: torch.Tensor | None) -> torch.Tensor:
+        return x.new_empty((*x.shape[:-1], w_q.shape[1]))
+
+    return qf_int8_linear, qf_int8_linear_fake
+
+
+def patch_int8_linear() -> bool:
+    """Small-M (decode) W8A8 linears -> B200 W8A16 kernel on the same int8 weights; large M keeps CUTLASS."""
+    from vllm.model_executor.kernels.linear.scaled_mm.cutlass import CutlassInt8ScaledMMLinearKernel
+    from vllm.utils.torch_utils import direct_register_custom_op
+
+    from .w8a16 import SMALL_M
+
+    orig_apply = CutlassInt8ScaledMMLinearKernel.apply_weights
+    if getattr(orig_apply, "_qwen_fastpath", False):
+        return False
+
+    op, fake = make_int8_linear_op()
+    if not hasattr(torch.ops.vllm, "qf_int8_linear"):
+        direct_register_custom_op("qf_int8_linear", op, mutates_args=[], fake_impl=fake)
+
+    def apply_weights(self, layer, x, bias=None):
+        w_q, w_s, i_s, i_zp, azp_adj = self._get_layer_params(layer)
+        if i_s is None and i_zp is None and azp_adj is None:  # dynamic symmetric per-token activations
+            return torch.ops.vllm.qf_int8_linear(x, w_q, w_s, bias)
+        return orig_apply(self, layer, x, bias)
+
+    apply_weights._qwen_fastpath = True
+    apply_weights._qf_orig = orig_apply
+    CutlassInt8ScaledMMLinearKernel.apply_weights = apply_weights
+    logger.info("qwen_fastpath: B200 W8A16 decode path for W8A8-int8 linears (M <= %d), CUTLASS above", SMALL_M)
+    return True
+
+
+# ----------------------------------------------------------------------------------------------
+# QWEN_FAST_DRAFT_HEAD
+# ----------------------------------------------------------------------------------------------
+def quantize_head_rows(weight: torch.Tensor, block_rows: int = 16384):
+    """Per-row symmetric int8 copy of an lm_head weight ``[V, H]`` (patches.py:143-147): ``s = max|w| / 127``
+    (at least 1e-8 / 127), ``q = clamp(round_half_even(w / s), -127, 127)``, processed in 16384-row blocks so
+    the fp32 temporaries stay small.  Returns (int8 ``[V, H]``, fp32 ``[V]``) on the weight's device."""
+    V, H = weight.shape
+    w8 = torch.empty((V, H), dtype=torch.int8, device=weight.device)
+    scale = torch.empty((V,), dtype=torch.float32, device=weight.device)
+    with torch.no_grad():
+        for r0 in range(0, V, block_rows):
+            rows = weight[r0:r0 + block_rows].float()
+            s = rows.abs().amax(dim=1).clamp_(min=1e-8) / 127.0
+            w8[r0:r0 + block_rows] = torch.round(rows / s[:, None]).clamp_(-127, 127).to(torch.int8)
+            scale[r0:r0 + block_rows] = s
+    return w8, scale
+
+
+def attach_int8_head(draft_model) -> bool:
+    """Give a draft model (``Qwen3_5MTP``-like: ``lm_head.weight`` 2-D, ``lm_head.tp_size == 1``) its int8
+    head copy (patches.py:133-152).  Returns True if attached."""
+    lm_head = getattr(draft_model, "lm_head", None)
+    weight = getattr(lm_head, "weight", None)
+    if weight is None or weight.dim() != 2 or getattr(lm_head, "tp_size", 1) != 1:
+        return False
+    from .w8a16 import pick_config
+    V, H = weight.shape
+    w8, scale = quantize_head_rows(weight)
+    num_pad = lm_head.shard_indices.num_org_vocab_padding
+    draft_model._qf_head_i8 = (w8.t(), scale, num_pad, pick_config(V, H))
+    logger.info("qwen_fastpath: int8 draft lm_head (%d x %d, %.2f GB) for MTP proposals", V, H, w8.numel() / 1e9)
+    return True
+
+
+def int8_head(model, hidden_states: torch.Tensor, want_logits: bool = True):
+    """Run the int8 head if the model and inputs qualify (patches.py:157-166); else None.
+
+    Returns (logits bf16 [M, V] or None, row_max, row_argmax (+ vocab start), row_lse)."""
+    from .w8a16 import SMALL_M, w8a16_head
+    q = model.__dict__.get("_qf_head_i8")
+    lp = getattr(model, "logits_processor", None)
+    if (q is None or lp is None or hidden_states.dim() != 2 or hidden_states.shape[0] > SMALL_M
+            or hidden_states.shape[0] < 1 or hidden_states.dtype != torch.bfloat16 or lp.logits_as_input
+            or lp.soft_cap is not None or lp.scale != 1.0
+            or getattr(model, "draft_id_to_target_id", None) is not None):
+        return None
+    w_t, scale, num_pad, cfg = q
+    if cfg is None:
+        return None
+    si = model.lm_head.shard_indices
+    V = w_t.shape[1]
+    out = w8a16_head(hidden_states, w_t, scale, n_valid=V - num_pad, vocab_offset=si.org_vocab_start_index,
+                     want_logits=want_logits, pdl=True)
+    model._qf_head_stats = out[1:]
+    return out
+
+
+def patch_draft_lm_head() -> bool:
+    """MTP drafting through an int8 per-row copy of the lm_head: half the bytes of the bf16 head per draft
+    token, and argmax / logsumexp fused into the GEMM."""
+    try:
+        from vllm.model_executor.models import qwen3_5_mtp
+    except Exception as e:  # noqa: BLE001 -- any import failure of the host model disables only this patch
+        logger.info("qwen_fastpath: draft head patch skipped (%s)", e)
+        return False
+    cls = qwen3_5_mtp.Qwen3_5MTP
+    if getattr(cls.compute_logits, "_qwen_fastpath", False):
+        return False
+
+    try:
+        from vllm.v1.worker.gpu.spec_decode.mtp.speculator import MTPSpeculator
+    except Exception:  # noqa: BLE001
+        MTPSpeculator = None
+    if MTPSpeculator is not None:
+        orig_load = MTPSpeculator.load_draft_model
+        if not getattr(orig_load, "_qwen_fastpath", False):
+            def load_draft_model(self, target_model, target_attn_layer_names):
+                draft_model = orig_load(self, target_model, target_attn_layer_names)
+                if isinstance(draft_model, cls):
+                    attach_int8_head(draft_model)
+                return draft_model
+
+            load_draft_model._qwen_fastpath = True
+            MTPSpeculator.load_draft_model = load_draft_model
+    else:
+        logger.info("qwen_fastpath: this vLLM has no MTPSpeculator.load_draft_model hook; call "
+                    "patches.attach_int8_head(draft_model) after loading the drafter")
+
+    orig_logits = cls.compute_logits
+    orig_top = getattr(cls, "get_top_tokens", None)
+
+    def compute_logits(self, hidden_states, spec_step_idx=0):
+        out = int8_head(self, hidden_states)
+        if out is None:
+            return orig_logits(self, hidden_states, spec_step_idx)
+        return out[0][..., : self.logits_processor.org_vocab_size]
+
+    def get_top_tokens(self, hidden_states):
+        out = int8_head(self, hidden_states, want_logits=False)
+        if out is not None:
+            return out[2]
+        if orig_top is not None:
+            return orig_top(self, hidden_states)
+        logits = orig_logits(self, hidden_states)
+        si = self.lm_head.shard_indices
+        if si.num_org_vocab_padding > 0:
+            logits[..., -si.num_org_vocab_padding:] = -float("inf")
+        return logits.argmax(dim=-1) + si.org_vocab_start_index
+
+    compute_logits._qwen_fastpath = True
+    get_top_tokens._qwen_fastpath = True
+    cls.compute_logits = compute_logits
+    cls.get_top_tokens = get_top_tokens
+    logger.info("qwen_fastpath: int8 draft lm_head enabled")
+    return True

@@ -1,0 +1,198 @@
+"""Small-M W8A16 GEMM over the int8 weights vLLM's W8A8 linear method already holds -- B200 host side.
+
+Mirrors ``qwen_fastpath.w8a16`` (plugin/qwen_fastpath/w8a16.py) of EurekaZang/qwen-a100-fastpath: the same
+``SMALL_M``, ``pick_config(N, K)`` and ``w8a16_mm(x, w_t, w_scale, cfg, out_dtype)`` surface, with the
+Triton kernel replaced by the sm_100a CUDA library ``libqf_b200.so`` (C ABI in include/qf_b200.h):
+
+* the weight tensor is read in place: vLLM's ``w_q`` is the checkpoint's int8 ``[N, K]`` row-major viewed as
+  ``[K, N]`` with stride ``(1, K)`` (no repacking, no extra weight memory, w8a16.py:7);
+* ``y = (x @ w) * scale`` with exact bf16 x int8 products, fp32 accumulation, one rounding to ``out_dtype``
+  (w8a16.py:28-38); split-K runs inside one launch (no ``torch.zeros`` + cast, w8a16.py:78-83);
+* ``w8a16_head`` adds the fused per-row (max, argmax, logsumexp) of the int8 draft LM head.
+
+All tensors must be CUDA tensors; there is no CPU path.
+"""
+from __future__ import annotations
+
+import os
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import LIB, check
+
+SMALL_M = 16  # rows handled by the small-M path (w8a16.py:12); larger M keeps vLLM's int8 tensor-core GEMM
+
+# (BLOCK_M, BLOCK_N, BLOCK_K, SPLIT_K, num_warps, num_stages) in the reference's tuple order.  On B200 one
+# configuration serves every shape: 128 output channels x 128 k per pipeline stage, stream-K split over all
+# SMs (SPLIT_K = 0 means "chosen per launch by the stream-K partition"), 8 consumer warps + 1 TMA producer.
+B200_CONFIG = (16, 128, 128, 0, 9, 5)
+_PDL_DEFAULT = os.environ.get("QF_PDL", "0") == "1"
+
+
+def pick_config(N: int, K: int):
+    """Launch configuration for an ``[N, K]`` weight, or ``None`` if the small-M path cannot take it.
+
+    The reference's ``pick_config`` (w8a16.py:58-68) returns ``None`` unless ``K`` divides its block sizes;
+    the B200 kernel handles any ``K >= 1`` (TMA zero-fills the ragged edge), so ``None`` is returned only for
+    empty or oversized shapes.
+    """
+    if N < 1 or K < 1 or N > _lib.QF_MAX_N:
+        return None
+    return B200_CONFIG
+
+
+# ----------------------------------------------------------------------------------------------
+# workspace: one zero-initialised buffer per (device, stream); calls on a stream are ordered, so they
+# can share it.  Kernels leave its counters at zero.
+# ----------------------------------------------------------------------------------------------
+_ws_lock = threading.Lock()
+_ws: dict[tuple[int, int], torch.Tensor] = {}
+_MIN_WS = 8 << 20
+
+
+def workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream.cuda_stream)
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, _MIN_WS), dtype=torch.uint8, device=device)
+            _ws[key] = buf
+        return buf
+
+
+def workspace_status(device=None, stream=None) -> int:
+    """Read and clear the sticky device error flag of the current stream's workspace (synchronises)."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    stream = torch.cuda.current_stream(device) if stream is None else stream
+    key = (device.index, stream.cuda_stream)
+    buf = _ws.get(key)
+    if buf is None:
+        return _lib.QF_OK
+    import ctypes
+    st = ctypes.c_int(0)
+    check("qf_workspace_status", LIB.qf_workspace_status(buf.data_ptr(), stream.cuda_stream, ctypes.byref(st)))
+    return st.value
+
+
+def _aligned_rows(x: torch.Tensor) -> torch.Tensor:
+    """x [M, K] bf16 with unit column stride, 16-byte aligned base and row stride % 8 == 0 (TMA rules)."""
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if x.data_ptr() % 16 or (x.shape[0] > 1 and x.stride(0) % 8):
+        x = x.clone(memory_format=torch.contiguous_format)
+    return x
+
+
+def _check_weight(w_t: torch.Tensor, K: int) -> int:
+    if w_t.dtype != torch.int8 or w_t.dim() != 2 or w_t.stride(0) != 1:
+        raise ValueError("w_t must be int8 [K, N] with stride (1, ldw) (vLLM's transposed w_q view)")
+    if K == 0:
+        return 16
+    ldw = w_t.stride(1) if w_t.shape[1] > 1 else (K + 15) // 16 * 16
+    if w_t.data_ptr() % 16 or ldw % 16:
+        raise ValueError("w_t must be 16-byte aligned with a row stride that is a multiple of 16 bytes")
+    return ldw
+
+
+def weight_supported(w_t: torch.Tensor) -> bool:
+    """True if the int8 weight view satisfies the kernel's layout and alignment rules."""
+    if w_t.dtype != torch.int8 or w_t.dim() != 2 or w_t.stride(0) != 1 or not w_t.is_cuda:
+        return False
+    ldw = w_t.stride(1) if w_t.shape[1] > 1 else 16
+    return w_t.data_ptr() % 16 == 0 and ldw % 16 == 0
+
+
+def w8a16_mm(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, cfg=None, out_dtype=torch.bfloat16,
+             bias: torch.Tensor | None = None, out: torch.Tensor | None = None, pdl: bool | None = None):
+    """``x [M, K]`` bf16 (any row stride, unit column stride) @ ``w_t [K, N]`` int8 (stride ``(1, K)``), times
+    ``w_scale [N]`` fp32 -> ``[M, N]`` in ``out_dtype`` (bf16 or fp32).  Same contract as the reference's
+    ``w8a16_mm`` (w8a16.py:71-83).  ``bias`` (bf16 ``[N]``) is added as the reference's ``y + bias``
+    (patches.py:96-97): a second bf16 rounding.  ``out`` may supply the output tensor.  ``pdl`` launches with
+    programmatic dependent launch (weights must not be written by the previous kernel on the stream).
+    """
+    if x.dim() != 2:
+        raise ValueError("x must be 2-D [M, K]")
+    M, K = x.shape
+    N = w_t.shape[1]
+    if w_t.shape[0] != K:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} vs w_t {tuple(w_t.shape)}")
+    if M > SMALL_M:
+        raise ValueError(f"M={M} > {SMALL_M}: the small-M path handles at most {SMALL_M} rows")
+    if not (x.is_cuda and w_t.is_cuda and w_scale.is_cuda):
+        raise ValueError("libqf_b200 needs CUDA tensors (there is no CPU path)")
+    if x.dtype != torch.bfloat16:
+        raise ValueError("x must be bfloat16")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be torch.bfloat16 or torch.float32")
+    scale = w_scale.reshape(-1)
+    if scale.numel() != N or scale.dtype != torch.float32:
+        raise ValueError("w_scale must hold N fp32 per-channel scales")
+    scale = scale.contiguous()
+    if bias is not None:
+        if bias.numel() != N or bias.dtype != torch.bfloat16:
+            raise ValueError("bias must be bf16 [N]")
+        bias = bias.reshape(-1).contiguous()
+    ldw = _check_weight(w_t, K)
+    x = _aligned_rows(x)
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    elif out.shape != (M, N) or out.dtype != out_dtype or out.stride(-1) != 1:
+        raise ValueError("out must be [M, N] of out_dtype with unit column stride")
+    if M == 0 or N == 0:
+        return out
+    stream = torch.cuda.current_stream(x.device)
+    nbytes = LIB.qf_w8a16_workspace_bytes(M, N, K)
+    ws = workspace(x.device, stream, nbytes)
+    flags = _lib.QF_FLAG_PDL if (_PDL_DEFAULT if pdl is None else pdl) else 0
+    rc = LIB.qf_w8a16_gemm(x.data_ptr(), x.stride(0), w_t.data_ptr(), ldw, scale.data_ptr(),
+                           bias.data_ptr() if bias is not None else None, out.data_ptr(), out.stride(0),
+                           _lib.QF_DTYPE_F32 if out_dtype == torch.float32 else _lib.QF_DTYPE_BF16,
+                           M, N, K, ws.data_ptr(), ws.numel(), flags, stream.cuda_stream)
+    check("qf_w8a16_gemm", rc)
+    return out
+
+
+def w8a16_head(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, n_valid: int | None = None,
+               vocab_offset: int = 0, want_logits: bool = True, pdl: bool | None = None, out=None):
+    """Int8 draft LM head: bf16 logits ``[M, N]`` (or ``None``) and per-row statistics over columns
+    ``[0, n_valid)`` of those logits: ``(row_max fp32 [M], row_argmax int64 [M] (+ vocab_offset, first index on
+    ties), row_lse fp32 [M])``.  Same contraction as ``w8a16_mm``; replaces ``int8_logits`` /
+    ``get_top_tokens`` (plugin/qwen_fastpath/patches.py:157-185) without a second pass over the logits.
+    ``out`` may supply the four output tensors (logits may be None).
+    """
+    if x.dim() != 2:
+        raise ValueError("hidden states must be 2-D [M, K]")
+    M, K = x.shape
+    N = w_t.shape[1]
+    if w_t.shape[0] != K or M > SMALL_M or M < 1:
+        raise ValueError("bad head shapes")
+    if not (x.is_cuda and w_t.is_cuda and w_scale.is_cuda) or x.dtype != torch.bfloat16:
+        raise ValueError("head needs CUDA tensors and bf16 hidden states")
+    n_valid = N if n_valid is None else int(n_valid)
+    scale = w_scale.reshape(-1).contiguous()
+    if scale.numel() != N or scale.dtype != torch.float32:
+        raise ValueError("w_scale must hold N fp32 scales")
+    ldw = _check_weight(w_t, K)
+    x = _aligned_rows(x)
+    dev = x.device
+    if out is not None:
+        logits, row_max, row_arg, row_lse = out
+        if logits is not None and (logits.shape != (M, N) or logits.dtype != torch.bfloat16 or logits.stride(-1) != 1):
+            raise ValueError("logits must be bf16 [M, N] with unit column stride")
+    else:
+        logits = torch.empty((M, N), dtype=torch.bfloat16, device=dev) if want_logits else None
+        row_max = torch.empty((M,), dtype=torch.float32, device=dev)
+        row_arg = torch.empty((M,), dtype=torch.int64, device=dev)
+        row_lse = torch.empty((M,), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ws = workspace(dev, stream, LIB.qf_w8a16_workspace_bytes(M, N, K))
+    flags = _lib.QF_FLAG_PDL if (_PDL_DEFAULT if pdl is None else pdl) else 0
+    rc = LIB.qf_w8a16_head(x.data_ptr(), x.stride(0), w_t.data_ptr(), ldw, scale.data_ptr(),
+                           logits.data_ptr() if logits is not None else None,
+                           logits.stride(0) if logits is not None else N, M, N, K, n_valid,
+                           int(vocab_offset), row_max.data_ptr(), row_arg.data_ptr(), row_lse.data_ptr(),
+                           ws.data_ptr(), ws.numel(), flags, stream.cuda_stream)
+    check("qf_w8a16_head", rc)
+    return logits, row_max, row_arg, row_lse

@@ -1,0 +1,102 @@
+"""CUDA int8 draft LM head: bf16 logits + fused per-row (max, argmax, logsumexp) against the oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import w8a16_oracle as orc
+from tests.conftest import from_dev_bf16, to_dev_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def head(dev, x_bits, W, s, n_valid, offset, want_logits=True):
+    import torch
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_head
+    xt = to_dev_bf16(x_bits, dev)
+    wt = torch.from_numpy(W).to(dev).t()
+    st = torch.from_numpy(s).to(dev)
+    out = w8a16_head(xt, wt, st, n_valid=n_valid, vocab_offset=offset, want_logits=want_logits)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("V,H,M,pad,offset", [(1000, 256, 1, 0, 0), (4100, 512, 4, 36, 0), (3000, 1024, 3, 0, 12345),
+                                              (16384 + 640, 256, 16, 64, 0), (130, 128, 8, 2, 7)])
+def test_head_matches_oracle(dev, V, H, M, pad, offset):
+    x, W, s = orc.make_inputs(V + H + M, M, V, H)
+    logits, mx, am, lse = head(dev, x, W, s, V - pad, offset)
+    lg = from_dev_bf16(logits)
+    ref = orc.w8a16_mm(x, W, s, "bf16")
+    frac = np.mean(lg != ref)
+    assert frac < 0.01
+    # statistics are over the kernel's own bf16 logits: exact against numpy on them
+    mx_own, am_own, lse_own = orc.head_stats(lg, V - pad, offset)
+    assert np.array_equal(mx.cpu().numpy(), mx_own)
+    assert np.array_equal(am.cpu().numpy(), am_own)
+    np.testing.assert_allclose(lse.cpu().numpy(), lse_own, rtol=2e-6)
+    # and against the oracle's logits wherever the oracle's top-2 gap exceeds rounding noise
+    mx_r, am_r, lse_r = orc.head_stats(ref, V - pad, offset)
+    gap = orc.top2_gap(ref, V - pad)
+    ok = gap > 0
+    assert np.array_equal(am.cpu().numpy()[ok], am_r[ok])
+    np.testing.assert_allclose(lse.cpu().numpy(), lse_r, rtol=1e-5)
+
+
+def test_head_first_index_on_ties_and_padding(dev):
+    V, H, M = 2048, 256, 2
+    x, W, s = orc.make_inputs(5, M, V, H)
+    xf = orc.bf16_to_f32(x)
+    s[:] = np.float32(0.005)
+    hot = np.where(xf[0] >= 0, 127, -127).astype(np.int8)
+    for r in (700, 1500, 2040):        # identical top rows: first index wins; 2040 lies in the padding
+        W[r] = hot
+    logits, mx, am, lse = head(dev, x, W, s, n_valid=2000, offset=100)
+    assert am[0].item() == 700 + 100
+    lg = from_dev_bf16(logits)
+    assert lg[0, 700] == lg[0, 1500] == lg[0, 2040]
+    mx_own, am_own, lse_own = orc.head_stats(lg, 2000, 100)
+    assert np.array_equal(am.cpu().numpy(), am_own)
+    np.testing.assert_allclose(lse.cpu().numpy(), lse_own, rtol=2e-6)
+    assert np.array_equal(orc.top_tokens(lg, V - 2000, 100), am.cpu().numpy())  # get_top_tokens semantics
+
+
+def test_head_without_logits_store(dev):
+    V, H, M = 5000, 384, 4
+    x, W, s = orc.make_inputs(8, M, V, H)
+    full = head(dev, x, W, s, V, 0)
+    part = head(dev, x, W, s, V, 0, want_logits=False)
+    assert part[0] is None
+    for a, b in zip(full[1:], part[1:]):
+        assert np.array_equal(a.cpu().numpy(), b.cpu().numpy())
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+def test_full_vocab_config3(dev, M):
+    """Config 3 (vocab 151936 x 5120): statistics agree exactly with torch ops on the returned logits and the
+    logits with the reference's fp32 dequant-matmul."""
+    import torch
+    import torch.nn.functional as F
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_head
+    V, H = 151936, 5120
+    g = torch.Generator(device=dev).manual_seed(M)
+    W = torch.randint(-127, 128, (V, H), dtype=torch.int8, device=dev, generator=g)
+    s = torch.rand(V, device=dev, generator=g) * 0.009 + 0.001
+    x = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+    logits, mx, am, lse = w8a16_head(x, W.t(), s)
+    lf = logits.float()
+    assert torch.equal(am, lf.argmax(-1))
+    assert torch.equal(mx, lf.max(-1).values)
+    torch.testing.assert_close(lse, torch.logsumexp(lf.double(), -1).float(), rtol=2e-6, atol=0)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = torch.cat([F.linear(x.float(), W[i:i + 8192].float() * s[i:i + 8192, None]) for i in range(0, V, 8192)], 1)
+    assert ((lf - ref).norm() / ref.norm()).item() < 3e-3
+
+
+def test_head_deterministic(dev):
+    V, H, M = 151936 // 8, 5120, 4
+    x, W, s = orc.make_inputs(31, M, V, H)
+    a = head(dev, x, W, s, V, 0)
+    b = head(dev, x, W, s, V, 0)
+    for u, v in zip(a, b):
+        assert np.array_equal(u.cpu().numpy().view(np.uint8), v.cpu().numpy().view(np.uint8))

@@ -1,0 +1,99 @@
+"""The C-ABI library loads without a GPU, exports every entry point include/qf_b200.h declares, and rejects bad
+arguments with the documented codes before any CUDA call is made."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from qwen_a100_fastpath_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "qf_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(qf_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ("qf_w8a16_gemm", "qf_w8a16_head", "qf_w8a16_workspace_bytes", "qf_workspace_status"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    bound = {name for name, _, _ in _lib.SIGNATURES}
+    assert set(declared_functions()) <= bound, "every declared entry point has a ctypes signature"
+
+
+def test_abi_version_and_strerror():
+    assert _lib.LIB.qf_abi_version() == _lib.ABI_VERSION
+    assert _lib.LIB.qf_strerror(0) == b"ok"
+    assert _lib.LIB.qf_strerror(-4).startswith(b"alignment")
+    assert _lib.LIB.qf_strerror(12345) == b"unknown error"
+
+
+def test_workspace_bytes_layout():
+    small = _lib.LIB.qf_w8a16_workspace_bytes(1, 128, 128)
+    big = _lib.LIB.qf_w8a16_workspace_bytes(16, 151936, 5120)
+    assert 0 < small < big
+    assert big - small == (151936 // 128 - 1) * 256  # head statistics: 16 float4 per 128-row tile
+
+
+FAKE = 1 << 20  # a 16-byte-aligned non-null address; validation rejects before dereferencing anything
+
+
+def gemm(**kw):
+    a = dict(x=FAKE, ldx=5120, w=FAKE, ldw=5120, scale=FAKE, bias=None, y=FAKE, ldy=5120, y_dtype=0, M=4, N=5120,
+             K=5120, ws=FAKE, ws_bytes=1 << 30, flags=0, stream=None)
+    a.update(kw)
+    return _lib.LIB.qf_w8a16_gemm(*a.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(M=17), -2),                        # beyond the small-M path
+    (dict(M=-1), -2),
+    (dict(N=_lib.QF_MAX_N + 1), -2),
+    (dict(scale=None), -1),
+    (dict(ws=None), -1),
+    (dict(ws_bytes=1024), -6),
+    (dict(ldw=5000), -3),                    # ldw < K
+    (dict(ldx=100), -3),
+    (dict(ldw=5136 + 8), -4),                # ldw % 16 != 0
+    (dict(w=FAKE + 8), -4),
+    (dict(x=FAKE + 2), -4),
+    (dict(ldx=5124), -4),                    # ldx % 8 != 0
+    (dict(ws=FAKE + 16), -4),
+    (dict(y_dtype=7), -8),
+    (dict(y=None), -1),
+    (dict(ldy=10), -3),
+])
+def test_gemm_argument_validation(kw, code):
+    assert gemm(**kw) == code
+    assert len(_lib.LIB.qf_last_error_detail()) > 0
+
+
+def test_empty_problem_is_a_noop_without_cuda():
+    assert gemm(M=0) == 0
+    assert gemm(N=0) == 0
+
+
+def test_head_argument_validation():
+    f = _lib.LIB.qf_w8a16_head
+    args = [FAKE, 5120, FAKE, 5120, FAKE, FAKE, 151936, 4, 151936, 5120, 151936, 0, FAKE, FAKE, FAKE, FAKE,
+            1 << 30, 0, None]
+    bad_nvalid = list(args)
+    bad_nvalid[10] = 151937
+    assert f(*bad_nvalid) == -2
+    bad_stats = list(args)
+    bad_stats[13] = None
+    assert f(*bad_stats) == -1
+    k0 = list(args)
+    k0[9] = 0
+    assert f(*k0) == -2

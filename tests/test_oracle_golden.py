@@ -1,0 +1,146 @@
+"""Pin the CPU oracle to the reference: its outputs must match what the reference plugin's own code produced
+(tests/golden/reference_outputs.*, made by tests/golden/make_fixtures.py from plugin/qwen_fastpath)."""
+from __future__ import annotations
+
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import w8a16_oracle as orc
+
+GOLD = Path(__file__).resolve().parent / "golden"
+META = json.loads((GOLD / "reference_outputs.json").read_text())
+ARR = np.load(GOLD / "reference_outputs.npz")
+
+
+def sha(*arrays) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        a = np.ascontiguousarray(a)
+        h.update(str(a.dtype).encode() + str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()
+
+
+def bf16_close(a_bits, b_bits, max_mismatch_frac=0.01):
+    """bf16 tensors agree up to fp32 summation order: at most one ulp apart, and rarely differ at all."""
+    a = orc.bf16_to_f32(a_bits).astype(np.float64)
+    b = orc.bf16_to_f32(b_bits).astype(np.float64)
+    big = np.maximum(np.abs(a), np.abs(b)).astype(np.float32)
+    ulp = np.spacing(big).astype(np.float64) * 2.0 ** 16  # bf16 ulp = 2^16 fp32 ulps
+    diff = np.abs(a - b)
+    assert np.all(diff <= ulp + 1e-30), f"max diff {diff.max()} exceeds one bf16 ulp"
+    frac = np.mean(a_bits != b_bits)
+    assert frac <= max_mismatch_frac, f"{frac:.4%} of outputs differ"
+    return frac
+
+
+def gemm_inputs(c):
+    ldx = c["ldx"] if c["ldx"] != c["K"] else None
+    x, W, s = orc.make_inputs(c["seed"], c["M"], c["N"], c["K"], x_row_stride=ldx)
+    assert sha(x, W, s) == c["inputs_sha256"], "seeded input generator drifted from the fixture"
+    return x, W, s
+
+
+@pytest.mark.parametrize("case", META["gemm"], ids=lambda c: f"N{c['N']}_K{c['K']}_M{c['M']}")
+def test_w8a16_mm_matches_reference_kernel(case):
+    x, W, s = gemm_inputs(case)
+    y = orc.w8a16_mm(x, W, s, "bf16", K=case["K"])
+    bf16_close(y, ARR[f"gemm{case['case']}_y"])
+
+
+@pytest.mark.parametrize("case", META["gemm"], ids=lambda c: f"N{c['N']}_K{c['K']}_M{c['M']}")
+def test_reference_fp32_oracle_agrees(case):
+    """The reference's own fp32 oracle expression (bench/test_w8a16.py:15) is within its published error."""
+    x, W, s = gemm_inputs(case)
+    ref = orc.dequant_matmul_f32(x, W, s, K=case["K"])
+    y = orc.bf16_to_f32(ARR[f"gemm{case['case']}_y"])
+    rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
+    assert rel < 3e-3  # bf16 output rounding; the reference reports 0.0016-0.0017 (data/measurements.json:419-437)
+
+
+@pytest.mark.parametrize("case", [c for c in META["linear"]], ids=lambda c: f"lin{c['case']}")
+def test_qf_int8_linear_matches_reference(case):
+    M = int(np.prod(case["lead"]))
+    x, W, s = orc.make_inputs(case["seed"], M, case["N"], case["K"])
+    assert sha(x, W, s) == case["inputs_sha256"]
+    if M > META["small_m"]:
+        assert case["path"].startswith("fallback"), "M > 16 must leave the small-M path"
+        return
+    assert case["path"] == "w8a16"
+    bias = orc.make_bias(case["bias_seed"], case["N"]) if case["bias"] else None
+    y = orc.qf_int8_linear(x.reshape(*case["lead"], case["K"]), W, s, bias)
+    assert list(y.shape) == case["out_shape"]
+    bf16_close(y, ARR[f"linear{case['case']}_y"])
+
+
+def head_weight():
+    h = META["head"]
+    rs = np.random.RandomState(h["weight_seed"])
+    wf = rs.standard_normal((h["V"], h["H"])).astype(np.float32) * 0.05
+    wf[7] = 0.0
+    wf[11, 3] = 40.0
+    wb = orc.f32_to_bf16(wf)
+    assert sha(wb) == h["weight_sha256"]
+    return wb
+
+
+def test_draft_head_quantizer_bit_exact():
+    q, s = orc.quantize_rows(head_weight())
+    rows = ARR["head_w8_row_index"]
+    assert np.array_equal(q[rows], ARR["head_w8_rows"])
+    assert sha(q) == META["head"]["w8_sha256"]
+    assert np.array_equal(s.view(np.uint32), ARR["head_scale"].view(np.uint32))
+
+
+@pytest.mark.parametrize("case", META["head"]["cases"], ids=lambda c: f"M{c['M']}")
+def test_draft_head_logits_and_top_tokens(case):
+    h = META["head"]
+    q, s = orc.quantize_rows(head_weight())
+    hs = orc.f32_to_bf16(np.random.RandomState(case["seed"]).standard_normal((case["M"], h["H"])).astype(np.float32))
+    logits = orc.w8a16_mm(hs, q, s, "bf16")
+    ref_logits = ARR[f"head{case['case']}_logits"]
+    org = h["V"] - h["num_pad"]
+    assert list(ref_logits.shape) == [case["M"], org]          # compute_logits slices to org_vocab_size
+    bf16_close(logits[:, :org], ref_logits)
+    top = orc.top_tokens(logits, h["num_pad"], 0)
+    assert np.array_equal(top, ARR[f"head{case['case']}_top"])
+    mx, am, lse = orc.head_stats(logits, org, 0)
+    assert np.array_equal(am, top)
+    assert np.all(np.isfinite(lse)) and np.all(lse >= mx)
+
+
+def test_pick_config_reference_table_recorded():
+    """The reference's heuristic covers every BASELINE shape (none is in its A100 TUNED table) and rejects
+    K = 100; the B200 build accepts any K (documented gate difference)."""
+    pc = META["pick_config"]
+    assert pc["64,100"] is None
+    assert pc["5120,8192"] == [16, 32, 256, 4, 4, 3]
+    from qwen_a100_fastpath_b200.w8a16 import pick_config
+    assert pick_config(64, 100) is not None and pick_config(0, 5) is None
+
+
+def test_tp_combine_matches_unsharded():
+    """Vocab-sharded (max, argmax, lse) gathered in rank order equals the unsharded statistics."""
+    rs = np.random.RandomState(5)
+    logits = orc.f32_to_bf16(rs.standard_normal((3, 4096)).astype(np.float32) * 4)
+    logits[1, 100] = logits[1, 3000] = orc.f32_to_bf16(np.float32(50.0))  # a cross-shard tie
+    full = orc.head_stats(logits, 4096)
+    for world in (2, 4, 8):
+        n = 4096 // world
+        parts = [orc.head_stats(logits[:, r * n:(r + 1) * n], n, r * n) for r in range(world)]
+        mx, am, lse = orc.combine_head_stats(parts)
+        assert np.array_equal(mx, full[0]) and np.array_equal(am, full[1])
+        np.testing.assert_allclose(lse, full[2], rtol=1e-12)
+    assert full[1][1] == 100
+
+
+def test_row_parallel_partials_sum_to_full():
+    x, W, s = orc.make_inputs(9, 5, 256, 1024)
+    full = orc.dequant_matmul_f64(x, W, s)
+    for world in (2, 4, 8):
+        acc = sum(orc.dequant_matmul_f64(*reversed(orc.shard_rows(W, x, r, world)), s) for r in range(world))
+        np.testing.assert_allclose(acc, full, rtol=1e-12, atol=1e-9)
