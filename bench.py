@@ -198,7 +198,7 @@ class Step:
             self.x[name] = torch.randn(M, k, device=dev, generator=g).to(torch.bfloat16)
             self.y[name] = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
         self.hidden = torch.randn(M, HEAD[2], device=dev, generator=g).to(torch.bfloat16)
-        self.logits = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
+        self.logits = torch.empty(M, self.head_n, device=dev, dtype=torch.bfloat16)
         self.row_max = torch.empty(M, device=dev, dtype=torch.float32)
         self.row_arg = torch.empty(M, device=dev, dtype=torch.int64)
         self.row_lse = torch.empty(M, device=dev, dtype=torch.float32)
@@ -206,7 +206,7 @@ class Step:
         self.gathered = torch.empty(world, M, 3, device=dev, dtype=torch.float64)
         self.launches_per_step = layers * len(LAYER) + 1
         self.bytes_rank = layers * sum(alg_bytes(*shard(N, K, st, world), M) for _, N, K, st in LAYER) + \
-            alg_bytes(n, HEAD[2], M, head=True)
+            alg_bytes(self.head_n, HEAD[2], M, head=True)
 
     def gemm_bytes(self, name: str) -> int:
         for nm, N, K, st in LAYER:

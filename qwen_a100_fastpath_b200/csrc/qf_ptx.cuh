@@ -103,6 +103,50 @@ __device__ __forceinline__ void mma_bf16_m16n8k16(float (&d)[4], uint32_t a0, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma_f16_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                 uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void lds64(uint32_t addr, uint32_t& a, uint32_t& b) {
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
+}
+__device__ __forceinline__ void sts64(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+
+// ---- exact int8 -> fp16 ----------------------------------------------------------------------------
+// Four signed bytes (k, k+1, k+2, k+3) -> a02 = f16x2{k, k+2}, a13 = f16x2{k+1, k+3}.
+// One lop3 builds, for bytes 0 and 2, the fp16 bit patterns 0x64uu with uu = byte ^ 0x80 (= byte + 128):
+// out = mask ? (w ^ C) : C with mask 0x00FF00FF and C = 0x64806480 (lut 0x6A), i.e. the fp16 values
+// 1024 + byte + 128; the same on w >> 8 gives bytes 1 and 3.  Subtracting 1152 leaves the byte exactly
+// (fp16 holds every integer up to 2048).  The pairing (k, k+2) / (k+1, k+3) is matched by the activation
+// layout the kernel builds.
+__device__ __forceinline__ void dequant_i8x4_f16(uint32_t w, uint32_t& a02, uint32_t& a13) {
+  uint32_t lo, hi;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(lo) : "r"(w), "r"(0x00FF00FFu), "r"(0x64806480u));
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(hi) : "r"(w >> 8), "r"(0x00FF00FFu), "r"(0x64806480u));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(a02) : "r"(lo), "r"(0x64806480u));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(a13) : "r"(hi), "r"(0x64806480u));
+}
+
+// Two bf16x2 words (x0, x1), (x2, x3) -> f16x2 (x0, x2), (x1, x3), the activation pairing of
+// dequant_i8x4_f16.  Returns non-zero if any value is outside the fp16 range (|x| >= 65536, Inf, NaN):
+// the magnitude bits plus 0x3880 reach bit 15 exactly when they are >= 0x4780 (bf16 65536).
+__device__ __forceinline__ uint32_t bf16x4_to_f16_pairs(uint32_t w0, uint32_t w1, uint32_t& o0, uint32_t& o1) {
+  const float x0 = __uint_as_float(w0 << 16), x1 = __uint_as_float(w0 & 0xFFFF0000u);
+  const float x2 = __uint_as_float(w1 << 16), x3 = __uint_as_float(w1 & 0xFFFF0000u);
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(o0) : "f"(x2), "f"(x0));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(o1) : "f"(x3), "f"(x1));
+  const uint32_t t0 = (w0 & 0x7FFF7FFFu) + 0x38803880u;
+  const uint32_t t1 = (w1 & 0x7FFF7FFFu) + 0x38803880u;
+  return (t0 | t1) & 0x80008000u;
+}
+
 // ---- exact int8 -> bf16 ---------------------------------------------------------------------------
 // Four signed bytes (k, k+1, k+2, k+3) -> lo = bf16x2{k, k+1}, hi = bf16x2{k+2, k+3}.
 // Each byte b is biased to u = b + 128 (xor 0x80), placed in the low mantissa byte of the fp32 2^23

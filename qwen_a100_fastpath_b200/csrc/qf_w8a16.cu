@@ -37,6 +37,7 @@
 #include <climits>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -48,14 +49,17 @@ namespace qf {
 
 constexpr int kBN = 128;                    // output channels per tile
 constexpr int kBK = 128;                    // k per stage (int8 bytes of one swizzled weight-box row)
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kConsumerWarps = 16;          // two per 16-row m-tile (one per k-chunk parity)
+constexpr int kMTiles = kBN / 16;
+constexpr int kProducerWarp = kConsumerWarps;       // TMA issue (one lane)
+constexpr int kConverterWarp = kConsumerWarps + 1;  // bf16 -> fp16 activations of each stage
+constexpr int kThreads = (kConsumerWarps + 2) * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kWStageBytes = kBN * kBK;     // 16 KiB
 constexpr int kMaxGrid = 256;
 constexpr int kMaxTiles = QF_MAX_N / kBN;   // tile-counter capacity
-constexpr int kBarPairBase = 1;             // named barriers 1..4: warp pairs; 5: all consumers
-constexpr int kBarConsumers = 5;
+constexpr int kBarPairBase = 1;             // named barriers 1..8: warp pairs of an m-tile; 9: all consumers
+constexpr int kBarConsumers = 9;
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;  // 4 s
 
 // workspace layout (bytes); the prefix [0, kWsZeroBytes) must be zero before the first call
@@ -70,14 +74,17 @@ template <int NT> struct Cfg {
   static constexpr int kStages = NT == 1 ? 5 : 4;
   static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT rows][64 bf16]
   static constexpr int kXStageBytes = 2 * kXBoxBytes;
+  static constexpr int kXPairs = kXStageBytes / 8;              // 8-byte blocks converted to fp16 per stage
   static constexpr int kOffX = kStages * kWStageBytes;
-  static constexpr int kOffRed = kOffX + kStages * kXStageBytes;
-  static constexpr int kRedBytes = kConsumerWarps * 32 * 4 * NT * 4;
+  static constexpr int kOffX16 = kOffX + kStages * kXStageBytes;
+  static constexpr int kOffRed = kOffX16 + kStages * kXStageBytes;
+  static constexpr int kRedBytes = (kMTiles * 32 * 4 * NT * 4) > (kConsumerWarps * 16 * 16)
+                                       ? kMTiles * 32 * 4 * NT * 4 : kConsumerWarps * 16 * 16;
   static constexpr int kOffStat = kOffRed + kRedBytes;
-  static constexpr int kStatBytes = kConsumerWarps * 16 * 16;   // float4 per (warp, token)
-  static constexpr int kOffBar = kOffStat + kStatBytes;
-  static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;
-  static constexpr int kSmemBytes = kOffFlag + 16 + 1024;       // + alignment slack
+  static constexpr int kStatBytes = kMTiles * 16 * 16;          // float4 per (m-tile, token)
+  static constexpr int kOffBar = kOffStat + kStatBytes;         // full[S], empty[S], xready[S]
+  static constexpr int kOffFlag = kOffBar + 3 * kStages * 8;    // abort, last, inexact[S]
+  static constexpr int kSmemBytes = kOffFlag + 8 + 4 * kStages + 1024;  // + alignment slack
   static constexpr uint32_t kTxBytes = kWStageBytes + kXStageBytes;
 };
 
@@ -98,6 +105,7 @@ struct Params {
   float* row_max;
   long long* row_argmax;
   float* row_lse;
+  int f16_path;  // 1: convert activations to fp16 per stage (cheaper weight dequant); 0: exact bf16 path
 };
 
 struct RowStat {
@@ -160,8 +168,37 @@ __device__ __forceinline__ void store_out(const Params& p, int n, int m, float v
   }
 }
 
+// One 16-k chunk (16 bytes of each of the rows g and g+8) of the lane's m-tile: four m16n8k16 MMAs per token
+// tile.  xa / xb hold the 16 activations of the same k (words 0-3 and 4-7) for each token tile.
+template <int NT, bool F16>
+__device__ __forceinline__ void mma_chunk(float (&acc)[NT][4], const uint4& ra, const uint4& rb, const uint4 (&xa)[NT],
+                                          const uint4 (&xb)[NT]) {
+  const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
+  const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+  for (int kq = 0; kq < 4; ++kq) {
+    uint32_t a0, a1, a2, a3;
+    if constexpr (F16) {
+      dequant_i8x4_f16(wa[kq], a0, a2);
+      dequant_i8x4_f16(wb[kq], a1, a3);
+    } else {
+      dequant_i8x4_bf16(wa[kq], a0, a2);
+      dequant_i8x4_bf16(wb[kq], a1, a3);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint32_t b0 = kq == 0 ? xa[nt].x : kq == 1 ? xa[nt].z : kq == 2 ? xb[nt].x : xb[nt].z;
+      const uint32_t b1 = kq == 0 ? xa[nt].y : kq == 1 ? xa[nt].w : kq == 2 ? xb[nt].y : xb[nt].w;
+      if constexpr (F16)
+        mma_f16_m16n8k16(acc[nt], a0, a1, a2, a3, b0, b1);
+      else
+        mma_bf16_m16n8k16(acc[nt], a0, a1, a2, a3, b0, b1);
+    }
+  }
+}
+
 template <int NT, bool HEAD>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     w8a16_streamk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                          const Params p) {
   using C = Cfg<NT>;
@@ -170,12 +207,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
   uint8_t* sX = smem + C::kOffX;
+  uint8_t* sX16 = smem + C::kOffX16;
   float* sRed = reinterpret_cast<float*>(smem + C::kOffRed);
   float4* sStat = reinterpret_cast<float4*>(smem + C::kOffStat);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  uint64_t* empty_bar = full_bar + S;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kOffBar);  // TMA bytes of the stage landed
+  uint64_t* empty_bar = full_bar + S;                                   // all consumer warps read the stage
+  uint64_t* xready_bar = empty_bar + S;                                 // fp16 activations of the stage written
   volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffFlag);
   volatile int* sLast = sAbort + 1;
+  volatile int* sInexact = sAbort + 2;  // [S]: an activation of the stage is outside the fp16 range
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -183,11 +223,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int it_begin = static_cast<int>(split_start(cta, p.T, p.G));
   const int it_end = static_cast<int>(split_start(cta + 1, p.T, p.G));
   const int n_iter = it_end - it_begin;
+  const bool use_f16 = p.f16_path != 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kConsumerThreads);
+      mbar_init(&empty_bar[s], kConsumerWarps);  // one arrival per consumer warp
+      mbar_init(&xready_bar[s], 1);              // the converter warp's lane 0
+      sInexact[s] = 0;
     }
     *sAbort = 0;
     *sLast = 0;
@@ -196,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ producer (one lane)
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
@@ -251,16 +294,49 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
 
-  // -------------------------------------------------------------------- consumers (8 warps)
+  if (warp == kConverterWarp) {
+    // ------------------------------------------------------------------ activation converter (one warp)
+    // bf16 -> fp16 of each landed stage, 8-byte blocks per lane, same offsets in the fp16 buffer with pairs
+    // permuted to (k, k+2), (k+1, k+3); flags the stage if a value is outside the fp16 range.
+    if (!use_f16) return;
+    pdl_wait();
+    const uint32_t sX_u32 = smem_u32(sX), sX16_u32 = smem_u32(sX16);
+    for (int i = 0; i < n_iter; ++i) {
+      const int st = i % S;
+      if (!mbar_wait_bounded(&full_bar[st], static_cast<uint32_t>(i / S) & 1u, sAbort)) {
+        if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
+        *sAbort = 1;
+      }
+      uint32_t bad = 0;
+#pragma unroll
+      for (int j = 0; j < C::kXPairs / 32; ++j) {
+        const uint32_t off = static_cast<uint32_t>(st * C::kXStageBytes + (lane + 32 * j) * 8);
+        uint32_t w0, w1, o0, o1;
+        lds64(sX_u32 + off, w0, w1);
+        bad |= bf16x4_to_f16_pairs(w0, w1, o0, o1);
+        sts64(sX16_u32 + off, o0, o1);
+      }
+      const bool any_bad = __any_sync(0xffffffffu, bad != 0);
+      __syncwarp();
+      if (lane == 0) {
+        sInexact[st] = any_bad ? 1 : 0;
+        mbar_arrive(&xready_bar[st]);  // release: the warp's fp16 stores and the flag
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers (16 warps)
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
-  const int q = warp >> 1;
-  const int h = warp & 1;
+  const int q = warp >> 1;   // m-tile: rows [16q, 16q + 16) of the 128-row tile
+  const int h = warp & 1;    // which half of the 16-byte k chunks of each stage
   const int g = lane >> 2;
   const int t = lane & 3;
   const int c = (t ^ h) | ((t & 1) << 2);  // this lane's 16-k chunk of each stage
   const uint32_t sW_u32 = smem_u32(sW);
   const uint32_t sX_u32 = smem_u32(sX);
-  const uint32_t w_off = static_cast<uint32_t>((32 * q + g) * 128 + ((c ^ g) << 4));
+  const uint32_t sX16_u32 = smem_u32(sX16);
+  const uint32_t w_off = static_cast<uint32_t>((16 * q + g) * 128 + ((c ^ g) << 4));
   const uint32_t x_off = static_cast<uint32_t>((c >> 2) * C::kXBoxBytes + g * 128);
   const uint32_t x_u0 = static_cast<uint32_t>(((2 * (c & 3)) ^ g) << 4);
   const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
@@ -269,112 +345,97 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* partials = reinterpret_cast<float*>(p.ws + kWsPartials);
   float4* tile_stats = reinterpret_cast<float4*>(p.ws + kWsStats);
   const int first_tile = it_begin / p.kiters;
-  const int ctid = threadIdx.x;  // 0..255 among consumers
+  const int ctid = threadIdx.x;  // 0..511 among consumers
 
-  float acc[2][NT][4];
+  float acc[NT][4];
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[j][nt][e] = 0.f;
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
+  int tile = first_tile;
+  int kk = it_begin - first_tile * p.kiters;
   for (int i = 0; i < n_iter; ++i) {
     const int s = i % S;
-    if (!mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, sAbort)) {
+    if (!mbar_wait_bounded(use_f16 ? &xready_bar[s] : &full_bar[s], static_cast<uint32_t>(i / S) & 1u, sAbort)) {
       if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
       *sAbort = 1;
     }
-    // activations: 16 consecutive k of rows g (and g + 8) of this lane's chunk
-    uint32_t xf[NT][8];
+    const bool f16 = use_f16 && sInexact[s] == 0;
+    const uint32_t xbase = (f16 ? sX16_u32 : sX_u32) + s * C::kXStageBytes + x_off;
+    uint4 xa[NT], xb[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const uint32_t base = sX_u32 + s * C::kXStageBytes + x_off + nt * 1024;
-      const uint4 v0 = lds128(base + x_u0);
-      const uint4 v1 = lds128(base + x_u1);
-      xf[nt][0] = v0.x; xf[nt][1] = v0.y; xf[nt][2] = v0.z; xf[nt][3] = v0.w;
-      xf[nt][4] = v1.x; xf[nt][5] = v1.y; xf[nt][6] = v1.z; xf[nt][7] = v1.w;
+      xa[nt] = lds128(xbase + nt * 1024 + x_u0);
+      xb[nt] = lds128(xbase + nt * 1024 + x_u1);
     }
-    uint4 wr[2][2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t base = sW_u32 + s * kWStageBytes + w_off + j * 2048;
-      wr[j][0] = lds128(base);
-      wr[j][1] = lds128(base + 1024);
-    }
-    mbar_arrive(&empty_bar[s]);  // release semantics: the loads above are performed before the slot is reused
-
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t wa[4] = {wr[j][0].x, wr[j][0].y, wr[j][0].z, wr[j][0].w};
-      const uint32_t wb[4] = {wr[j][1].x, wr[j][1].y, wr[j][1].z, wr[j][1].w};
-#pragma unroll
-      for (int kq = 0; kq < 4; ++kq) {
-        uint32_t a0, a1, a2, a3;
-        dequant_i8x4_bf16(wa[kq], a0, a2);
-        dequant_i8x4_bf16(wb[kq], a1, a3);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_bf16_m16n8k16(acc[j][nt], a0, a1, a2, a3, xf[nt][2 * kq], xf[nt][2 * kq + 1]);
-      }
-    }
+    const uint32_t wbase = sW_u32 + s * kWStageBytes + w_off;
+    const uint4 ra = lds128(wbase);
+    const uint4 rb = lds128(wbase + 1024);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);  // release: this warp's reads of the slot are done
+    if (f16)
+      mma_chunk<NT, true>(acc, ra, rb, xa, xb);
+    else
+      mma_chunk<NT, false>(acc, ra, rb, xa, xb);
 
     // ------------------------------------------------------------ tile epilogue
-    const int gi = it_begin + i;
-    const int tile = gi / p.kiters;
-    const int kk = gi - tile * p.kiters;
-    if (kk != p.kiters - 1 && i != n_iter - 1) continue;
+    const int cur_tile = tile;
+    const bool tile_end = (kk == p.kiters - 1) || (i == n_iter - 1);
+    if (++kk == p.kiters) {
+      kk = 0;
+      ++tile;
+    }
+    if (!tile_end) continue;
 
-    // combine the two k-halves held by warps (q, 0) and (q, 1): warp h keeps m-tile h
+    // fold the two k-halves of m-tile q held by warps (q, 0) and (q, 1) into warp (q, 0)
+    float v[NT][4];
     {
-      float* mine = sRed + (warp * 32 + lane) * 4 * NT;
+      float* slot = sRed + (q * 32 + lane) * 4 * NT;
+      if (h == 1) {
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) mine[nt * 4 + e] = acc[1 - h][nt][e];
+          for (int e = 0; e < 4; ++e) slot[nt * 4 + e] = acc[nt][e];
+      }
       named_bar_sync(kBarPairBase + q, 64);
-      const float* other = sRed + ((warp ^ 1) * 32 + lane) * 4 * NT;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[h][nt][e] += other[nt * 4 + e];
+        for (int e = 0; e < 4; ++e) v[nt][e] = acc[nt][e] + slot[nt * 4 + e];
       named_bar_sync(kBarPairBase + q, 64);
     }
-    float v[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[nt][e] = acc[h][nt][e];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][nt][e] = 0.f;
+      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
-    const int rl0 = 32 * q + 16 * h + g;  // local rows rl0 and rl0 + 8
-    const int tile_it0 = tile * p.kiters;
+    const int rl0 = 16 * q + g;  // local rows rl0 and rl0 + 8, owned by warp (q, 0) from here on
+    const int tile_it0 = cur_tile * p.kiters;
     const bool whole = (tile_it0 >= it_begin) && (tile_it0 + p.kiters <= it_end);
     bool finish = whole;
     if (!whole) {
-      const int which = (tile == first_tile) ? 0 : 1;
-      float* slot = partials + static_cast<size_t>(2 * cta + which) * kPartialSlotFloats;
+      if (h == 0) {
+        const int which = (cur_tile == first_tile) ? 0 : 1;
+        float* slot = partials + static_cast<size_t>(2 * cta + which) * kPartialSlotFloats;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int col = 8 * nt + 2 * t;
-        *reinterpret_cast<float2*>(slot + rl0 * 16 + col) = make_float2(v[nt][0], v[nt][1]);
-        *reinterpret_cast<float2*>(slot + (rl0 + 8) * 16 + col) = make_float2(v[nt][2], v[nt][3]);
+        for (int nt = 0; nt < NT; ++nt) {
+          const int col = 8 * nt + 2 * t;
+          *reinterpret_cast<float2*>(slot + rl0 * 16 + col) = make_float2(v[nt][0], v[nt][1]);
+          *reinterpret_cast<float2*>(slot + (rl0 + 8) * 16 + col) = make_float2(v[nt][2], v[nt][3]);
+        }
+        __threadfence();
       }
-      __threadfence();
       named_bar_sync(kBarConsumers, kConsumerThreads);
       if (ctid == 0) {
         const int c_first = cta_of(tile_it0, p.T, p.G);
         const int c_last = cta_of(min(tile_it0 + p.kiters, p.T) - 1, p.T, p.G);
-        const int old = atomicAdd(&counters[tile], 1);
+        const int old = atomicAdd(&counters[cur_tile], 1);
         *sLast = (old == c_last - c_first) ? 1 : 0;
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
       finish = *sLast != 0;
-      if (finish) {
+      if (finish && h == 0) {
         __threadfence();
         const int c_first = cta_of(tile_it0, p.T, p.G);
         const int c_last = cta_of(min(tile_it0 + p.kiters, p.T) - 1, p.T, p.G);
@@ -384,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
         for (int cc = c_first; cc <= c_last; ++cc) {
           const int ft = static_cast<int>(split_start(cc, p.T, p.G) / p.kiters);
-          const float* sl = partials + static_cast<size_t>(2 * cc + (tile == ft ? 0 : 1)) * kPartialSlotFloats;
+          const float* sl = partials + static_cast<size_t>(2 * cc + (cur_tile == ft ? 0 : 1)) * kPartialSlotFloats;
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const int col = 8 * nt + 2 * t;
@@ -393,55 +454,61 @@ __global__ void __launch_bounds__(kThreads, 2)
             v[nt][0] += a.x; v[nt][1] += a.y; v[nt][2] += b.x; v[nt][3] += b.y;
           }
         }
-        if (ctid == 0) counters[tile] = 0;  // ready for the next call on this workspace
+        if (ctid == 0) counters[cur_tile] = 0;  // ready for the next call on this workspace
       }
     }
     if (!finish) continue;
 
-    const int n0 = tile * kBN + rl0;
+    const int n0 = cur_tile * kBN + rl0;
     const int n1 = n0 + 8;
-    const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
-    const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
     if constexpr (!HEAD) {
+      if (h == 0) {
+        const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
+        const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int m0 = 8 * nt + 2 * t;
-        store_out(p, n0, m0, v[nt][0] * s0);
-        store_out(p, n0, m0 + 1, v[nt][1] * s0);
-        store_out(p, n1, m0, v[nt][2] * s1);
-        store_out(p, n1, m0 + 1, v[nt][3] * s1);
+        for (int nt = 0; nt < NT; ++nt) {
+          const int m0 = 8 * nt + 2 * t;
+          store_out(p, n0, m0, v[nt][0] * s0);
+          store_out(p, n0, m0 + 1, v[nt][1] * s0);
+          store_out(p, n1, m0, v[nt][2] * s1);
+          store_out(p, n1, m0 + 1, v[nt][3] * s1);
+        }
       }
     } else {
       // bf16 logits, then per-token statistics of this tile over the same bf16 values
+      if (h == 0) {
+        const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
+        const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
+        for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          const int m = 8 * nt + 2 * t + b;
-          const __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][b] * s0);
-          const __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + b] * s1);
-          if (p.logits && m < p.M) {
-            if (n0 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n0] = r0;
-            if (n1 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n1] = r1;
+          for (int b = 0; b < 2; ++b) {
+            const int m = 8 * nt + 2 * t + b;
+            const __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][b] * s0);
+            const __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + b] * s1);
+            if (p.logits && m < p.M) {
+              if (n0 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n0] = r0;
+              if (n1 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n1] = r1;
+            }
+            RowStat st{-INFINITY, INT_MAX, 0.f};
+            if (n0 < p.n_valid) st = RowStat{__bfloat162float(r0), n0, 1.f};
+            if (n1 < p.n_valid) st = stat_combine(st, RowStat{__bfloat162float(r1), n1, 1.f});
+            st = stat_combine(st, stat_shfl_xor(st, 4));
+            st = stat_combine(st, stat_shfl_xor(st, 8));
+            st = stat_combine(st, stat_shfl_xor(st, 16));
+            if (g == 0) sStat[q * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
           }
-          RowStat st{-INFINITY, INT_MAX, 0.f};
-          if (n0 < p.n_valid) st = RowStat{__bfloat162float(r0), n0, 1.f};
-          if (n1 < p.n_valid) st = stat_combine(st, RowStat{__bfloat162float(r1), n1, 1.f});
-          st = stat_combine(st, stat_shfl_xor(st, 4));
-          st = stat_combine(st, stat_shfl_xor(st, 8));
-          st = stat_combine(st, stat_shfl_xor(st, 16));
-          if (g == 0) sStat[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
         }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
       if (warp == 0) {
         if (lane < 8 * NT) {
           RowStat st{-INFINITY, INT_MAX, 0.f};
-          for (int w = 0; w < kConsumerWarps; ++w) {
+          for (int w = 0; w < kMTiles; ++w) {
             const float4 f = sStat[w * 16 + lane];
             st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
           }
-          tile_stats[static_cast<size_t>(tile) * 16 + lane] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
+          tile_stats[static_cast<size_t>(cur_tile) * 16 + lane] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
           __threadfence();
         }
         __syncwarp();
@@ -462,13 +529,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
 #pragma unroll
           for (int off = 1; off < 32; off <<= 1) st = stat_combine(st, stat_shfl_xor(st, off));
-          if (lane == 0) sStat[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
+          if (lane == 0) reinterpret_cast<float4*>(sRed)[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
         }
         named_bar_sync(kBarConsumers, kConsumerThreads);
         if (warp == 0 && lane < p.M) {
           RowStat st{-INFINITY, INT_MAX, 0.f};
           for (int w = 0; w < kConsumerWarps; ++w) {
-            const float4 f = sStat[w * 16 + lane];
+            const float4 f = reinterpret_cast<const float4*>(sRed)[w * 16 + lane];
             st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
           }
           p.row_max[lane] = st.m;
@@ -477,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (ctid == 0) reinterpret_cast<unsigned*>(p.ws)[1] = 0u;
       }
-      named_bar_sync(kBarConsumers, kConsumerThreads);  // sStat / sLast reuse by the next tile
+      named_bar_sync(kBarConsumers, kConsumerThreads);  // sStat / sRed / sLast reuse by the next tile
     }
   }
 }
@@ -539,6 +606,26 @@ int device_info(int* dev_out, DeviceInfo** info_out) {
   return QF_OK;
 }
 
+// Optional upper bound on the stream-K grid (environment QF_GRID_CAP, read once): lets tests exercise other
+// split patterns, e.g. one CTA per whole problem.
+int grid_cap() {
+  static const int cap = [] {
+    const char* v = std::getenv("QF_GRID_CAP");
+    return v ? std::atoi(v) : 0;
+  }();
+  return cap;
+}
+
+// Activation path (environment QF_F16_PATH, read once): 1 (default) converts each stage's activations to
+// fp16 for the cheaper exact weight conversion; 0 keeps every stage on the bf16 path.
+int f16_path() {
+  static const int v = [] {
+    const char* e = std::getenv("QF_F16_PATH");
+    return e ? std::atoi(e) : 1;
+  }();
+  return v;
+}
+
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner,
               uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
   cuuint64_t dims[2] = {inner, rows};
@@ -576,11 +663,13 @@ int launch_streamk(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Par
                  xstride, 64, 8 * NT);
   if (rc) return rc;
 
+  p.f16_path = f16_path();
   p.kiters = (p.K + kBK - 1) / kBK;
   p.ntiles = (p.N + kBN - 1) / kBN;
   p.T = p.kiters * p.ntiles;
   int G = dinfo->sm_count;
   if (G > kMaxGrid) G = kMaxGrid;
+  if (grid_cap() > 0 && G > grid_cap()) G = grid_cap();
   if (G > p.T) G = p.T;
   p.G = G;
 

@@ -86,10 +86,12 @@ def _aligned_rows(x: torch.Tensor) -> torch.Tensor:
 
 
 def _check_weight(w_t: torch.Tensor, K: int) -> int:
-    if w_t.dtype != torch.int8 or w_t.dim() != 2 or w_t.stride(0) != 1:
-        raise ValueError("w_t must be int8 [K, N] with stride (1, ldw) (vLLM's transposed w_q view)")
+    if w_t.dtype != torch.int8 or w_t.dim() != 2:
+        raise ValueError("w_t must be int8 [K, N]")
     if K == 0:
         return 16
+    if w_t.stride(0) != 1:
+        raise ValueError("w_t must be int8 [K, N] with stride (1, ldw) (vLLM's transposed w_q view)")
     ldw = w_t.stride(1) if w_t.shape[1] > 1 else (K + 15) // 16 * 16
     if w_t.data_ptr() % 16 or ldw % 16:
         raise ValueError("w_t must be 16-byte aligned with a row stride that is a multiple of 16 bytes")

@@ -1,8 +1,9 @@
 """CUDA W8A16 GEMM (libqf_b200 via the C ABI) against the CPU oracle and the reference's golden outputs.
 
-Tolerances (north star): bf16 outputs within one bf16 ulp of the oracle's correctly rounded result and
-bit-identical for >= 99 % of elements (max relative error far below 2e-2); the fp32 export (accumulator x
-scale before rounding) within 1e-3 relative of the fp64 exact product (observed ~1e-6).
+Tolerances (north star): every bf16 output within one bf16 ulp of the oracle's correctly rounded result plus
+2^-16 * max|y| (the fp32 accumulation noise of cancelling partial sums), >= 99 % of outputs bit-identical,
+max relative error <= 2e-2 (observed ~1e-3, i.e. one ulp); the fp32 export (accumulator x scale before
+rounding) within 1e-3 relative of the fp64 exact product (observed 2e-7 .. 9e-7).
 """
 from __future__ import annotations
 
@@ -25,8 +26,12 @@ def bf16_close(a_bits, b_bits, max_mismatch_frac=0.01):
     b = orc.bf16_to_f32(b_bits).astype(np.float64)
     big = np.maximum(np.abs(a), np.abs(b)).astype(np.float32)
     ulp = np.spacing(big).astype(np.float64) * 2.0 ** 16
+    # one bf16 ulp, plus the fp32 accumulation noise of the partial sums (outputs near zero come from
+    # cancelling sums ~|y|max; their absolute error is set by those sums, not by their own ulp)
+    atol = 2.0 ** -16 * np.abs(b).max()
     diff = np.abs(a - b)
-    assert np.all(diff <= ulp), f"max diff {diff.max()} exceeds one bf16 ulp"
+    bad = diff > ulp + atol
+    assert not bad.any(), f"{int(bad.sum())} outputs beyond 1 ulp + {atol:.3g}; worst diff {diff[bad].max()}"
     frac = float(np.mean(np.asarray(a_bits) != np.asarray(b_bits)))
     assert frac <= max_mismatch_frac, f"{frac:.4%} of outputs differ from the oracle"
     rel = diff.max() / max(np.abs(b).max(), 1e-30)
@@ -196,3 +201,32 @@ def test_full_size_config2_against_torch_fp32(dev, name, N, K):
     assert rel32 < 1e-5, rel32
     assert rel16 < 3e-3, rel16                      # bf16 output rounding (reference reports 0.0016-0.0017)
     assert torch.equal(y16, y32.to(torch.bfloat16)) or (y16 != y32.to(torch.bfloat16)).float().mean() < 1e-3
+
+
+@pytest.mark.parametrize("M", [1, 5, 12])
+def test_activation_range_fallback(dev, M):
+    """Stages whose activations fall outside the fp16 range (|x| >= 65536, here up to 3e5) take the exact bf16
+    path; tiny activations (fp16 subnormal range) stay within the tolerance; results match the oracle."""
+    N, K = 1536, 3072
+    x, W, s = orc.make_inputs(900 + M, M, N, K)
+    xf = orc.bf16_to_f32(x).copy()
+    xf[0, 130] = 3.0e5          # k-stage 1 of row 0 falls back
+    xf[M - 1, 2900] = -7.0e4    # last stage
+    xf[:, 1024:1100] *= 1e-6    # tiny values on the fp16 path
+    x2 = orc.f32_to_bf16(xf)
+    *_, y = run_case(dev, M, N, K, seed=0, x_bits=x2, W=W, s=s)
+    bf16_close(from_dev_bf16(y), orc.w8a16_mm(x2, W, s, "bf16"))
+    *_, y32 = run_case(dev, M, N, K, seed=0, x_bits=x2, W=W, s=s, out_dtype="f32")
+    ref = orc.dequant_matmul_f64(x2, W, s)
+    got = y32.cpu().numpy().astype(np.float64)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-5
+
+
+def test_nan_activation_propagates(dev):
+    N, K, M = 512, 1024, 3
+    x, W, s = orc.make_inputs(77, M, N, K)
+    x = x.copy()
+    x[1, 500] = 0x7FC0  # NaN in row 1 only
+    *_, y = run_case(dev, M, N, K, seed=0, x_bits=x, W=W, s=s)
+    yf = y.float().cpu().numpy()
+    assert np.isnan(yf[1]).all() and np.isfinite(yf[[0, 2]]).all()

@@ -31,8 +31,10 @@ def bf16_close(a_bits, b_bits, max_mismatch_frac=0.01):
     b = orc.bf16_to_f32(b_bits).astype(np.float64)
     big = np.maximum(np.abs(a), np.abs(b)).astype(np.float32)
     ulp = np.spacing(big).astype(np.float64) * 2.0 ** 16  # bf16 ulp = 2^16 fp32 ulps
+    atol = 2.0 ** -16 * np.abs(b).max()  # fp32 accumulation noise of cancelling partial sums
     diff = np.abs(a - b)
-    assert np.all(diff <= ulp + 1e-30), f"max diff {diff.max()} exceeds one bf16 ulp"
+    bad = diff > ulp + atol
+    assert not bad.any(), f"{int(bad.sum())} outputs beyond 1 ulp + {atol:.3g}; worst diff {diff[bad].max()}"
     frac = np.mean(a_bits != b_bits)
     assert frac <= max_mismatch_frac, f"{frac:.4%} of outputs differ"
     return frac
