@@ -49,8 +49,12 @@ namespace qf {
 
 constexpr int kBN = 128;                    // output channels per tile
 constexpr int kBK = 128;                    // k per stage (int8 bytes of one swizzled weight-box row)
-constexpr int kConsumerWarps = 16;          // two per 16-row m-tile (one per k-chunk parity)
-constexpr int kMTiles = kBN / 16;
+#ifndef QF_MT_PER_WARP
+#define QF_MT_PER_WARP 1
+#endif
+constexpr int kMTiles = kBN / 16;                     // 16-row MMA tiles per 128-row tile
+constexpr int kJ = QF_MT_PER_WARP;                    // m-tiles per consumer warp
+constexpr int kConsumerWarps = 2 * kMTiles / kJ;      // each m-tile group is shared by two warps (k halves)
 constexpr int kProducerWarp = kConsumerWarps;       // TMA issue (one lane)
 constexpr int kConverterWarp = kConsumerWarps + 1;  // bf16 -> fp16 activations of each stage
 constexpr int kThreads = (kConsumerWarps + 2) * 32;
@@ -78,8 +82,8 @@ template <int NT> struct Cfg {
   static constexpr int kOffX = kStages * kWStageBytes;
   static constexpr int kOffX16 = kOffX + kStages * kXStageBytes;
   static constexpr int kOffRed = kOffX16 + kStages * kXStageBytes;
-  static constexpr int kRedBytes = (kMTiles * 32 * 4 * NT * 4) > (kConsumerWarps * 16 * 16)
-                                       ? kMTiles * 32 * 4 * NT * 4 : kConsumerWarps * 16 * 16;
+  static constexpr int kRedBytes = (kConsumerWarps * 32 * 4 * NT * 4) > (kConsumerWarps * 16 * 16)
+                                       ? kConsumerWarps * 32 * 4 * NT * 4 : kConsumerWarps * 16 * 16;
   static constexpr int kOffStat = kOffRed + kRedBytes;
   static constexpr int kStatBytes = kMTiles * 16 * 16;          // float4 per (m-tile, token)
   static constexpr int kOffBar = kOffStat + kStatBytes;         // full[S], empty[S], xready[S]
@@ -328,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 
   // -------------------------------------------------------------------- consumers (16 warps)
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
-  const int q = warp >> 1;   // m-tile: rows [16q, 16q + 16) of the 128-row tile
+  const int q = warp >> 1;   // m-tile group: rows [16*kJ*q, 16*kJ*(q + 1)) of the 128-row tile
   const int h = warp & 1;    // which half of the 16-byte k chunks of each stage
   const int g = lane >> 2;
   const int t = lane & 3;
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
   const uint32_t sW_u32 = smem_u32(sW);
   const uint32_t sX_u32 = smem_u32(sX);
   const uint32_t sX16_u32 = smem_u32(sX16);
-  const uint32_t w_off = static_cast<uint32_t>((16 * q + g) * 128 + ((c ^ g) << 4));
+  const uint32_t w_off = static_cast<uint32_t>((16 * kJ * q + g) * 128 + ((c ^ g) << 4));
   const uint32_t x_off = static_cast<uint32_t>((c >> 2) * C::kXBoxBytes + g * 128);
   const uint32_t x_u0 = static_cast<uint32_t>(((2 * (c & 3)) ^ g) << 4);
   const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
@@ -347,11 +351,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
   const int first_tile = it_begin / p.kiters;
   const int ctid = threadIdx.x;  // 0..511 among consumers
 
-  float acc[NT][4];
+  float acc[kJ][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+  for (int j = 0; j < kJ; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][nt][e] = 0.f;
 
   int tile = first_tile;
   int kk = it_begin - first_tile * p.kiters;
@@ -370,14 +376,21 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
       xb[nt] = lds128(xbase + nt * 1024 + x_u1);
     }
     const uint32_t wbase = sW_u32 + s * kWStageBytes + w_off;
-    const uint4 ra = lds128(wbase);
-    const uint4 rb = lds128(wbase + 1024);
+    uint4 ra[kJ], rb[kJ];
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) {
+      ra[j] = lds128(wbase + j * 2048);
+      rb[j] = lds128(wbase + j * 2048 + 1024);
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);  // release: this warp's reads of the slot are done
-    if (f16)
-      mma_chunk<NT, true>(acc, ra, rb, xa, xb);
-    else
-      mma_chunk<NT, false>(acc, ra, rb, xa, xb);
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) {
+      if (f16)
+        mma_chunk<NT, true>(acc[j], ra[j], rb[j], xa, xb);
+      else
+        mma_chunk<NT, false>(acc[j], ra[j], rb[j], xa, xb);
+    }
 
     // ------------------------------------------------------------ tile epilogue
     const int cur_tile = tile;
@@ -388,34 +401,41 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     }
     if (!tile_end) continue;
 
-    // fold the two k-halves of m-tile q held by warps (q, 0) and (q, 1) into warp (q, 0)
+    // fold the two k-halves held by warps (q, 0) and (q, 1): with one m-tile per warp, warp (q, 0) keeps it;
+    // with two, warp (q, h) keeps m-tile h of the group
     float v[NT][4];
+    const int keep = kJ == 1 ? 0 : h;      // which of this warp's m-tiles it finishes
+    const bool owner = kJ == 1 ? (h == 0) : true;
     {
-      float* slot = sRed + (q * 32 + lane) * 4 * NT;
-      if (h == 1) {
+      float* mine = sRed + ((kJ == 1 ? q : warp) * 32 + lane) * 4 * NT;
+      if (kJ == 1 ? (h == 1) : true) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) slot[nt * 4 + e] = acc[nt][e];
+          for (int e = 0; e < 4; ++e) mine[nt * 4 + e] = (kJ == 1 || keep == 1) ? acc[0][nt][e] : acc[kJ - 1][nt][e];
       }
       named_bar_sync(kBarPairBase + q, 64);
+      const float* other = kJ == 1 ? mine : sRed + ((warp ^ 1) * 32 + lane) * 4 * NT;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[nt][e] = acc[nt][e] + slot[nt * 4 + e];
+        for (int e = 0; e < 4; ++e) v[nt][e] = (keep == 0 ? acc[0][nt][e] : acc[kJ - 1][nt][e]) + other[nt * 4 + e];
       named_bar_sync(kBarPairBase + q, 64);
     }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int j = 0; j < kJ; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[j][nt][e] = 0.f;
 
-    const int rl0 = 16 * q + g;  // local rows rl0 and rl0 + 8, owned by warp (q, 0) from here on
+    const int mt = kJ * q + keep;  // m-tile finished by this warp (if owner)
+    const int rl0 = 16 * mt + g;   // local rows rl0 and rl0 + 8
     const int tile_it0 = cur_tile * p.kiters;
     const bool whole = (tile_it0 >= it_begin) && (tile_it0 + p.kiters <= it_end);
     bool finish = whole;
     if (!whole) {
-      if (h == 0) {
+      if (owner) {
         const int which = (cur_tile == first_tile) ? 0 : 1;
         float* slot = partials + static_cast<size_t>(2 * cta + which) * kPartialSlotFloats;
 #pragma unroll
@@ -435,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
       finish = *sLast != 0;
-      if (finish && h == 0) {
+      if (finish && owner) {
         __threadfence();
         const int c_first = cta_of(tile_it0, p.T, p.G);
         const int c_last = cta_of(min(tile_it0 + p.kiters, p.T) - 1, p.T, p.G);
@@ -462,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     const int n0 = cur_tile * kBN + rl0;
     const int n1 = n0 + 8;
     if constexpr (!HEAD) {
-      if (h == 0) {
+      if (owner) {
         const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
         const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
 #pragma unroll
@@ -476,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
       }
     } else {
       // bf16 logits, then per-token statistics of this tile over the same bf16 values
-      if (h == 0) {
+      if (owner) {
         const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
         const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
 #pragma unroll
@@ -496,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
             st = stat_combine(st, stat_shfl_xor(st, 4));
             st = stat_combine(st, stat_shfl_xor(st, 8));
             st = stat_combine(st, stat_shfl_xor(st, 16));
-            if (g == 0) sStat[q * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
+            if (g == 0) sStat[mt * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
           }
         }
       }
@@ -822,3 +842,4 @@ const char* qf_last_error_detail(void) { return g_err.c_str(); }
 int qf_abi_version(void) { return QF_ABI_VERSION; }
 
 }  // extern "C"
+
