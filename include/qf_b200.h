@@ -86,6 +86,23 @@ int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
                   float* row_max, int64_t* row_argmax, float* row_lse,
                   void* ws, size_t ws_bytes, unsigned flags, void* stream);
 
+/* Small-M W8A16 GEMM that allocates nothing and takes no workspace.  No counterpart in the reference: it is
+ * for callers that cannot allocate device memory themselves -- a host that embeds only this library through
+ * the C ABI (a Go, Java or C binding with no device allocator of its own), or a latency-critical path that
+ * must not call cudaMalloc, which can synchronise the device.  Same arguments and math as qf_w8a16_gemm
+ * without ws / ws_bytes.  Its scratch (split-tile counters and fp32 partial tiles) is a fixed
+ * QF_NOALLOC_SCRATCH_BYTES array inside the library, held by every GPU that loads the library until the
+ * process exits; N is limited to QF_NOALLOC_MAX_N (larger N returns QF_ERR_SHAPE).  The first call on a device
+ * looks up that array's device address (cudaGetSymbolAddress) and must be made with the device current,
+ * before any stream capture.  Every call clears the scratch's counters with one cudaMemsetAsync on `stream`.
+ * All calls share the one array, so calls whose kernels overlap on the GPU (different streams) race: order
+ * them on one stream. */
+#define QF_NOALLOC_MAX_N 65536
+#define QF_NOALLOC_SCRATCH_BYTES 2655232u
+int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
+                          const void* bias, void* y, int64_t ldy, int y_dtype, int M, int N, int K,
+                          unsigned flags, void* stream);
+
 /* Reads and clears the workspace's sticky device error flag (synchronises `stream`).  *status receives
  * QF_OK or QF_ERR_TIMEOUT.  Not for the hot path. */
 int qf_workspace_status(void* ws, void* stream, int* status);

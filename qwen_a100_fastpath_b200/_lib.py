@@ -17,6 +17,7 @@ QF_DTYPE_F32 = 1
 QF_MAX_M = 16
 QF_MAX_N = 1048576
 QF_FLAG_PDL = 1
+QF_NOALLOC_MAX_N = 65536
 ABI_VERSION = 1
 
 # (name, restype, argtypes) -- one entry per function declared in include/qf_b200.h
@@ -30,6 +31,9 @@ SIGNATURES = [
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int,
       _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
       _c.c_size_t, _c.c_uint, _c.c_void_p]),
+    ("qf_w8a16_gemm_noalloc", _c.c_int,
+     [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64,
+      _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_uint, _c.c_void_p]),
     ("qf_workspace_status", _c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(_c.c_int)]),
     ("qf_strerror", _c.c_char_p, [_c.c_int]),
     ("qf_last_error_detail", _c.c_char_p, []),

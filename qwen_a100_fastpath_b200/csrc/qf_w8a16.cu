@@ -843,3 +843,92 @@ int qf_abi_version(void) { return QF_ABI_VERSION; }
 
 }  // extern "C"
 
+// ================================================================================== allocation-free entry
+// qf_w8a16_gemm_noalloc: the same stream-K GEMM with its scratch (split-tile counters and fp32 partial tiles)
+// in a fixed array of this library instead of a caller-provided workspace, for callers that cannot allocate
+// device memory themselves (a host that embeds only this library and has no device allocator, e.g. a Go or
+// Java binding over the C ABI, or a latency-critical path that must not call cudaMalloc, which can
+// synchronise the device).  The array lives in every GPU that loads the library until the process exits.
+namespace qf {
+namespace {
+
+constexpr int kNoAllocMaxGrid = 160;                 // CTAs: partial-tile slots are 2 per CTA
+constexpr size_t kNoAllocBytes = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kNoAllocMaxGrid;
+static_assert(kNoAllocBytes == QF_NOALLOC_SCRATCH_BYTES, "header value out of date");
+
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch array for the current device, looked up once per device (with that device
+// current).  The host-side symbol is only a stand-in, never a device address.
+int noalloc_scratch(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) return fail(QF_ERR_LAUNCH, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return QF_OK;
+}
+
+}  // namespace
+}  // namespace qf
+
+extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
+                                     const void* bias, void* y, int64_t ldy, int y_dtype, int M, int N, int K,
+                                     unsigned flags, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(QF_ERR_SHAPE, "negative size");
+  if (M > QF_MAX_M) return fail(QF_ERR_SHAPE, "M > 16: the small-M path handles at most 16 rows");
+  if (N > QF_NOALLOC_MAX_N)
+    return fail(QF_ERR_SHAPE, "N above QF_NOALLOC_MAX_N (65536): the fixed scratch of the allocation-free entry "
+                              "point holds tile counters for at most that many output channels");
+  if (M == 0 || N == 0) return QF_OK;
+  if (!scale || !y) return fail(QF_ERR_INVALID, "null scale or y");
+  if (y_dtype != QF_DTYPE_BF16 && y_dtype != QF_DTYPE_F32) return fail(QF_ERR_DTYPE, "y_dtype must be bf16 or fp32");
+  if (M > 1 && ldy < N) return fail(QF_ERR_STRIDE, "ldy < N");
+  if (K > 0) {
+    if (!x || !w) return fail(QF_ERR_INVALID, "null x or w");
+    if (ldw < K) return fail(QF_ERR_STRIDE, "ldw < K");
+    if (M > 1 && ldx < K) return fail(QF_ERR_STRIDE, "ldx < K");
+    if (reinterpret_cast<uintptr_t>(w) % 16 || ldw % 16)
+      return fail(QF_ERR_ALIGN, "w must be 16-byte aligned with ldw % 16 == 0");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || (M > 1 && ldx % 8))
+      return fail(QF_ERR_ALIGN, "x must be 16-byte aligned with ldx % 8 == 0");
+  }
+  int dev;
+  DeviceInfo* dinfo;
+  int rc = device_info(&dev, &dinfo);
+  if (rc) return rc;
+  if (dinfo->sm_count > kNoAllocMaxGrid)
+    return fail(QF_ERR_SHAPE, "device has more SMs than the allocation-free scratch provides partial-tile slots for");
+  void* scratch = nullptr;
+  rc = noalloc_scratch(dev, &scratch);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: clear the error word and this call's tile counters.
+  const size_t ntiles = (static_cast<size_t>(N) + kBN - 1) / kBN;
+  cudaError_t e = cudaMemsetAsync(scratch, 0, kWsCounters + sizeof(int) * ntiles, st);
+  if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  Params p = {};
+  p.scale = scale;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = y;
+  p.ldy = ldy;
+  p.y_f32 = y_dtype == QF_DTYPE_F32;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ws = static_cast<uint8_t*>(scratch);
+  if (K == 0) {
+    const int64_t total = static_cast<int64_t>(M) * N;
+    fill_empty_k_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(p);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
+  }
+  if (M <= 8) return launch_streamk<1, false>(x, ldx, w, ldw, p, dinfo, flags, st);
+  return launch_streamk<2, false>(x, ldx, w, ldw, p, dinfo, flags, st);
+}
