@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
     ap.add_argument("--sweep-out", default="")
+    ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head: a few "
+                    "launches of each at --m (the small case for an ncu capture), then exit")
     return ap.parse_args()
 
 
@@ -202,7 +204,6 @@ class Step:
         self.row_max = torch.empty(M, device=dev, dtype=torch.float32)
         self.row_arg = torch.empty(M, device=dev, dtype=torch.int64)
         self.row_lse = torch.empty(M, device=dev, dtype=torch.float32)
-        self.stats = torch.empty(M, 3, device=dev, dtype=torch.float64)
         self.gathered = torch.empty(world, M, 3, device=dev, dtype=torch.float64)
         self.launches_per_step = layers * len(LAYER) + 1
         self.bytes_rank = layers * sum(alg_bytes(*shard(N, K, st, world), M) for _, N, K, st in LAYER) + \
@@ -218,6 +219,7 @@ class Step:
         """Enqueue the step.  ``linear(x, w_t, s) -> y`` replaces the GEMM call (the public op allocates its
         output); ``events`` records a CUDA event after every launch (instrumented pass)."""
         torch = self.torch
+        from qwen_a100_fastpath_b200 import tp
         from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_mm
         if events is not None:
             events[0].record()
@@ -233,23 +235,17 @@ class Step:
                     events[e].record()
                     e += 1
                 if style == "row" and self.world > 1:
-                    torch.distributed.all_reduce(y)
+                    tp.all_reduce_partial(y)
         w, s = self.head_w
         w8a16_head(self.hidden, w, s, n_valid=self.head_n, vocab_offset=self.rank * self.head_n, pdl=self.pdl,
                    out=(self.logits, self.row_max, self.row_arg, self.row_lse))
         if events is not None:
             events[e].record()
         if self.world > 1:
-            self.stats[:, 0] = self.row_max
-            self.stats[:, 1] = self.row_arg
-            self.stats[:, 2] = self.row_lse
-            torch.distributed.all_gather_into_tensor(self.gathered, self.stats)
-            mx = self.gathered[:, :, 0].max(0).values
-            cand = torch.where(self.gathered[:, :, 0] == mx, self.gathered[:, :, 1],
-                               torch.full_like(mx, float("inf")))
-            self.row_arg.copy_(cand.min(0).values.to(torch.int64))
+            mx, am, lse = tp.gather_head_stats(self.row_max, self.row_arg, self.row_lse, out=self.gathered)
             self.row_max.copy_(mx)
-            self.row_lse.copy_(torch.logsumexp(self.gathered[:, :, 2], 0))
+            self.row_arg.copy_(am)
+            self.row_lse.copy_(lse)
 
 
 def time_graph(graph, stream, steps, warmup, sampler=None):
@@ -504,6 +500,30 @@ def run_sweep(args, local: int):
         Path(args.sweep_out).write_text(json.dumps(rows, indent=1))
 
 
+def run_profile_gemm(args, local: int):
+    """Two launches of each named GEMM (int8 weights U[-127,127], distinct per launch) at M = --m."""
+    import torch
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_mm
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shapes = {nm: (N, K) for nm, N, K, _ in LAYER + [HEAD]}
+    g = torch.Generator(device=dev).manual_seed(3)
+    for name in args.profile_gemm.split(","):
+        N, K = shapes[name]
+        x = torch.randn(args.m, K, device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(2):
+            W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+            s = torch.rand(N, device=dev, generator=g) * 0.009 + 0.001
+            torch.cuda.synchronize()
+            if name == "lm_head":
+                w8a16_head(x, W.t(), s)
+            else:
+                w8a16_mm(x, W.t(), s, None, torch.bfloat16)
+            torch.cuda.synchronize()
+            del W
+    print("profile-gemm done:", args.profile_gemm)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -517,6 +537,10 @@ def main():
     if args.sweep:
         if rank == 0:
             run_sweep(args, local)
+        return
+    if args.profile_gemm:
+        if rank == 0:
+            run_profile_gemm(args, local)
         return
     run_ours(args, rank, world, local)
 
