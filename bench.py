@@ -367,7 +367,7 @@ def run_ours(args, rank: int, world: int, local: int):
         head_bytes = alg_bytes(st.head_n, HEAD[2], args.m, head=True)
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                    "kernel": "w8a16_streamk_kernel<NT=1> (qkv/o_proj/gate_up/down launches of the step)",
+                    "kernel": "w8a16_kernel<BN, NT=1> (qkv/o_proj/gate_up/down launches of the step)",
                     "bytes_per_launch": round(gemm_bytes), "us_per_launch": round(per_launch_ms * 1e3, 3),
                     "peak_source": peak_src + ", 'of measured'", "frac_of_nominal_8TBs": round(achieved / NOMINAL_HBM_GBS, 4),
                     "traffic_source": tsrc,

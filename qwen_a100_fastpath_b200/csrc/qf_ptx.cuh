@@ -82,6 +82,10 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Signal barrier `id` without waiting (the waiting side uses named_bar_sync with the same count).
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 // ---- shared / global loads ---------------------------------------------------------------------
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {

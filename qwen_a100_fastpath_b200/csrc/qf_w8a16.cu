@@ -8,27 +8,31 @@
 //
 // The contraction streams N*K int8 weight bytes once and is bound by HBM bandwidth at these M.  Design:
 //
-// * Stream-K split: the iteration space (tile of 128 output channels) x (128-wide k stage) is cut into
-//   G <= #SM equal contiguous ranges, one persistent CTA each, so every shape fills all SMs with no tail.
-//   Tiles that straddle CTAs are reduced by the CTA that finishes last (fp32 partials in the workspace,
-//   summed in CTA order, so results are deterministic), and the tile counter is reset for the next call.
-//   No memset or cast launches (the reference zero-fills an fp32 buffer and casts, w8a16.py:78-79, :83).
-// * One producer warp issues TMA loads (cp.async.bulk.tensor, 128-byte swizzle) of the weight box
-//   [128 rows x 128 bytes] and of the two activation boxes [8*NT rows x 64 bf16] of a stage into a
-//   mbarrier ring.  Weights carry an L2 evict-first hint; activations evict-last (every CTA reads them).
-//   With programmatic dependent launch the weight boxes of the first stages are issued before
-//   griddepcontrol.wait, i.e. while the previous kernel on the stream is still running.
-// * Eight consumer warps: warp (q, h) owns rows [32q, 32q+32) of the tile and half of the 16-byte k
-//   chunks of each stage.  Lane (g, t) takes chunk c = (t ^ h) | ((t & 1) << 2): with the 128B swizzle this
-//   makes both the weight reads (16 B of rows g and g+8) and the activation reads conflict-free.  Weights
-//   are converted int8 -> bf16 exactly in registers and fed to mma.sync m16n8k16 as the 16-row A operand
-//   ("swap AB"); the M <= 16 tokens are the 8-column B operand (NT = 1 or 2 column tiles).  The k order
-//   inside a chunk is permuted identically for A and B, which leaves the dot product unchanged.
-// * Epilogue: fp32 accumulator * scale, one rounding to bf16 (or fp32 export), optional bias as a second
-//   bf16 rounding exactly like the reference's `y + bias`.  The head epilogue also reduces the bf16 logits
-//   of each tile to per-row (max, first argmax, sum exp) and the last tile to finish folds all tiles.
+// * Tiles of BN output channels (BN = 128, 64 or 32, picked per shape so that there are at least as many tiles
+//   as SMs) and pipeline stages of BN x KS weight bytes (KS = 16384 / BN: a stage is always 16 KiB, i.e. 128,
+//   256 or 512 contiguous bytes of each weight row).  One persistent CTA per SM.
+// * Data-parallel + stream-K schedule: with ntiles = q*G + r, every CTA owns q whole tiles ("DP") and an equal
+//   share of the r * kiters stages of the remaining r tiles ("SK").  Each CTA runs its SK share first: the SK
+//   tiles' partial sums are handed to a fixup warp that reduces them (fp32 partials in the workspace, summed in
+//   CTA order, so results are deterministic) while the consumer warps stream the DP tiles.  No split reduction
+//   sits at the end of the kernel, and no memset or cast launches are needed (the reference zero-fills an fp32
+//   buffer for atomics and casts afterwards, w8a16.py:78-79, :83).
+// * One producer lane issues per stage B = KS/128 weight boxes [BN rows x 128 bytes] and 2B activation boxes
+//   [8*NT tokens x 64 bf16] (cp.async.bulk.tensor, 128-byte swizzle, no multicast) into a ring of up to 10
+//   stages guarded by mbarriers.  With programmatic dependent launch the weight boxes of the first stages are
+//   issued before griddepcontrol.wait, while the previous kernel on the stream still runs.
+// * Eight consumer warps.  Warp (u, h): unit u = (weight box b, pair of m-tiles mp), h = half of each box's
+//   16-byte k chunks; lane (g, t) takes chunk c = (t ^ h) | ((t & 1) << 2), which keeps both the swizzled weight
+//   reads and the activation reads free of bank conflicts.  Weights are converted to exact 16-bit floats in
+//   registers and fed to mma.sync m16n8k16 as the 16-row A operand ("swap AB"); the M <= 16 tokens are the
+//   8-column B operand (NT = 1 or 2 token tiles).  fp16 path: each warp converts its activation fragments
+//   bf16 -> fp16 (pairs (k, k+2), (k+1, k+3)) and the weights with one lop3 per byte pair; if any activation
+//   of the warp's chunk is outside the fp16 range the warp uses the exact bf16 conversion for that stage.
+// * Epilogue: fp32 accumulator * scale, one rounding to bf16 (or fp32 export), optional bias as the reference's
+//   second bf16 rounding (`y + bias`).  The head additionally reduces each tile's bf16 logits to per-row
+//   (max, first argmax, sum exp); the last CTA to finish folds all tiles in a fixed order.
 // * Every wait on an mbarrier is bounded (global timer); on expiry the CTA records QF_ERR_TIMEOUT in the
-//   workspace, stops waiting and drains its own TMA copies before exiting.
+//   workspace, stops waiting, and the producer drains its own TMA copies before the CTA exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -47,49 +51,54 @@
 
 namespace qf {
 
-constexpr int kBN = 128;                    // output channels per tile
-constexpr int kBK = 128;                    // k per stage (int8 bytes of one swizzled weight-box row)
-#ifndef QF_MT_PER_WARP
-#define QF_MT_PER_WARP 1
-#endif
-constexpr int kMTiles = kBN / 16;                     // 16-row MMA tiles per 128-row tile
-constexpr int kJ = QF_MT_PER_WARP;                    // m-tiles per consumer warp
-constexpr int kConsumerWarps = 2 * kMTiles / kJ;      // each m-tile group is shared by two warps (k halves)
-constexpr int kProducerWarp = kConsumerWarps;       // TMA issue (one lane)
-constexpr int kConverterWarp = kConsumerWarps + 1;  // bf16 -> fp16 activations of each stage
-constexpr int kThreads = (kConsumerWarps + 2) * 32;
+constexpr int kConsumerWarps = 8;
+constexpr int kProducerWarp = 8;            // TMA issue (one lane)
+constexpr int kFixupWarp = 9;               // reduction of stream-K partial tiles
+constexpr int kThreads = 10 * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kWStageBytes = kBN * kBK;     // 16 KiB
+constexpr int kWStageBytes = 16384;         // weight bytes per pipeline stage
+constexpr int kMaxBN = 128;
 constexpr int kMaxGrid = 256;
-constexpr int kMaxTiles = QF_MAX_N / kBN;   // tile-counter capacity
-constexpr int kBarPairBase = 1;             // named barriers 1..8: warp pairs of an m-tile; 9: all consumers
-constexpr int kBarConsumers = 9;
+constexpr int kMaxTiles = QF_MAX_N / kMaxBN;  // tile counters (tiles narrower than 128 rows only when N < 64*SMs)
+constexpr int kMaxSplit = 8;                // stream-K: at most about this many CTAs share a split tile
+constexpr int kBarConsumers = 1;            // named barriers (0 is __syncthreads)
+constexpr int kBarFix0 = 2;                 // consumers -> fixup warp, first partial SK tile
+constexpr int kBarFix1 = 3;                 // second partial SK tile
+constexpr int kBarEnd = 4;                  // consumers + fixup warp at the end (head only)
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;  // 4 s
 
 // workspace layout (bytes); the prefix [0, kWsZeroBytes) must be zero before the first call
-constexpr size_t kWsHeader = 256;                              // [0]: error flag, [1]: head tiles-done
+constexpr size_t kWsHeader = 256;                              // [0] error flag, [2] CTAs done (head)
 constexpr size_t kWsCounters = kWsHeader;                       // int32[kMaxTiles]
 constexpr size_t kWsZeroBytes = kWsCounters + sizeof(int) * kMaxTiles;
 constexpr size_t kWsPartials = (kWsZeroBytes + 1023) / 1024 * 1024;
-constexpr size_t kPartialSlotFloats = kBN * 16;                 // [128 rows][16 tokens]
+constexpr size_t kPartialSlotFloats = kMaxBN * 16;              // [BN rows][8*NT tokens]
 constexpr size_t kWsStats = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kMaxGrid;
 
-template <int NT> struct Cfg {
-  static constexpr int kStages = NT == 1 ? 5 : 4;
-  static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT rows][64 bf16]
-  static constexpr int kXStageBytes = 2 * kXBoxBytes;
-  static constexpr int kXPairs = kXStageBytes / 8;              // 8-byte blocks converted to fp16 per stage
+template <int BN, int NT> struct Geo {
+  static constexpr int KS = kWStageBytes / BN;                  // k bytes per stage: 128, 256, 512
+  static constexpr int B = KS / 128;                            // 128-byte weight boxes per stage
+  static constexpr int MT = BN / 16;                            // m-tiles per tile (8, 4, 2)
+  static constexpr int kWBoxBytes = BN * 128;
+  static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT tokens][64 bf16]
+  static constexpr int kXStageBytes = 2 * B * kXBoxBytes;
+  static constexpr int kStageBytes = kWStageBytes + kXStageBytes;
+  static constexpr int kRedBytes = kConsumerWarps * 2 * 32 * 4 * NT * 4;  // [warp][m-tile of pair][lane][4NT]
+  static constexpr int kStatBytes = 8 * 16 * 16;                          // float4 [m-tile][token]
+  static constexpr int kFixedBytes = kRedBytes + kStatBytes + 2 * 16 * 8 + 64 + 1024;
+  static constexpr int kBudget = 226 * 1024;
+  static constexpr int kStagesFit = (kBudget - kFixedBytes) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 10 ? 10 : kStagesFit;
   static constexpr int kOffX = kStages * kWStageBytes;
-  static constexpr int kOffX16 = kOffX + kStages * kXStageBytes;
-  static constexpr int kOffRed = kOffX16 + kStages * kXStageBytes;
-  static constexpr int kRedBytes = (kConsumerWarps * 32 * 4 * NT * 4) > (kConsumerWarps * 16 * 16)
-                                       ? kConsumerWarps * 32 * 4 * NT * 4 : kConsumerWarps * 16 * 16;
+  static constexpr int kOffRed = kOffX + kStages * kXStageBytes;
   static constexpr int kOffStat = kOffRed + kRedBytes;
-  static constexpr int kStatBytes = kMTiles * 16 * 16;          // float4 per (m-tile, token)
-  static constexpr int kOffBar = kOffStat + kStatBytes;         // full[S], empty[S], xready[S]
-  static constexpr int kOffFlag = kOffBar + 3 * kStages * 8;    // abort, last, inexact[S]
-  static constexpr int kSmemBytes = kOffFlag + 8 + 4 * kStages + 1024;  // + alignment slack
-  static constexpr uint32_t kTxBytes = kWStageBytes + kXStageBytes;
+  static constexpr int kOffBar = kOffStat + kStatBytes;       // full[S], empty[S]
+  static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;  // abort, last
+  static constexpr int kSmemBytes = kOffFlag + 64 + 1024;     // + alignment slack
+  static constexpr uint32_t kTxBytes = kStageBytes;
+  static_assert(MT / 2 * B == kConsumerWarps / 2, "eight warps cover the stage");
+  static_assert(kStages >= 4, "pipeline too shallow");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 struct Params {
@@ -99,8 +108,13 @@ struct Params {
   int64_t ldy;
   int y_f32;
   int M, N, K;
-  int kiters, ntiles, T, G;
+  int kiters, ntiles, G;
+  int q;       // whole (DP) tiles per CTA: tiles r + cta + j * G, j < q
+  int r;       // stream-K tiles 0 .. r-1
+  int Tsk;     // r * kiters stream-K stages, split over the first Gsk CTAs
+  int Gsk;
   uint8_t* ws;
+  int f16_path;
   // head
   __nv_bfloat16* logits;
   int64_t ldl;
@@ -109,7 +123,6 @@ struct Params {
   float* row_max;
   long long* row_argmax;
   float* row_lse;
-  int f16_path;  // 1: convert activations to fp16 per stage (cheaper weight dequant); 0: exact bf16 path
 };
 
 struct RowStat {
@@ -139,7 +152,7 @@ __device__ __forceinline__ RowStat stat_shfl_xor(const RowStat& v, int mask) {
 __device__ __forceinline__ long long split_start(int c, int T, int G) {
   return (static_cast<long long>(c) * T) / G;
 }
-// CTA whose range holds iteration i: largest c with split_start(c) <= i.
+// CTA whose (non-empty) range holds iteration i: largest c with split_start(c) <= i (requires G <= T).
 __device__ __forceinline__ int cta_of(int i, int T, int G) {
   return static_cast<int>(((static_cast<long long>(i) + 1) * G - 1) / T);
 }
@@ -172,8 +185,46 @@ __device__ __forceinline__ void store_out(const Params& p, int n, int m, float v
   }
 }
 
-// One 16-k chunk (16 bytes of each of the rows g and g+8) of the lane's m-tile: four m16n8k16 MMAs per token
-// tile.  xa / xb hold the 16 activations of the same k (words 0-3 and 4-7) for each token tile.
+// Walks a CTA's stages in order: its stream-K share of tiles 0..r-1, then its whole tiles.
+struct StageIter {
+  int tile, kk, i;
+  bool sk;
+  int n_sk, n_iter, sk_begin, sk_end;
+  __device__ __forceinline__ void init(const Params& p, int cta) {
+    if (cta < p.Gsk) {
+      sk_begin = static_cast<int>(split_start(cta, p.Tsk, p.Gsk));
+      sk_end = static_cast<int>(split_start(cta + 1, p.Tsk, p.Gsk));
+    } else {
+      sk_begin = sk_end = 0;
+    }
+    n_sk = sk_end - sk_begin;
+    n_iter = n_sk + p.q * p.kiters;
+    i = 0;
+    sk = n_sk > 0;
+    if (sk) {
+      tile = sk_begin / p.kiters;
+      kk = sk_begin - tile * p.kiters;
+    } else {
+      tile = p.r + cta;
+      kk = 0;
+    }
+  }
+  __device__ __forceinline__ void next(const Params& p) {
+    ++i;
+    if (++kk == p.kiters) {
+      kk = 0;
+      tile += sk ? 1 : p.G;
+    }
+    if (sk && i == n_sk) {
+      sk = false;
+      tile = p.r + static_cast<int>(blockIdx.x);
+      kk = 0;
+    }
+  }
+};
+
+// One 16-k chunk (16 bytes of each of the rows g and g+8 of an m-tile): four m16n8k16 MMAs per token tile.
+// xa / xb hold the 16 activations of the same k (words 0-3 and 4-7) for each token tile.
 template <int NT, bool F16>
 __device__ __forceinline__ void mma_chunk(float (&acc)[NT][4], const uint4& ra, const uint4& rb, const uint4 (&xa)[NT],
                                           const uint4 (&xb)[NT]) {
@@ -201,40 +252,45 @@ __device__ __forceinline__ void mma_chunk(float (&acc)[NT][4], const uint4& ra, 
   }
 }
 
-template <int NT, bool HEAD>
-__global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
-    w8a16_streamk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                         const Params p) {
-  using C = Cfg<NT>;
+// Statistics of one bf16 logit row pair (rows n0, n0 + 8 of a token column) reduced over the 8 lanes g.
+__device__ __forceinline__ RowStat warp_tile_stat(const Params& p, int n0, int n1, __nv_bfloat16 r0,
+                                                  __nv_bfloat16 r1) {
+  RowStat st{-INFINITY, INT_MAX, 0.f};
+  if (n0 < p.n_valid) st = RowStat{__bfloat162float(r0), n0, 1.f};
+  if (n1 < p.n_valid) st = stat_combine(st, RowStat{__bfloat162float(r1), n1, 1.f});
+  st = stat_combine(st, stat_shfl_xor(st, 4));
+  st = stat_combine(st, stat_shfl_xor(st, 8));
+  st = stat_combine(st, stat_shfl_xor(st, 16));
+  return st;
+}
+
+template <int BN, int NT, bool HEAD>
+__global__ void __launch_bounds__(kThreads, 1)
+    w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                 const Params p) {
+  using C = Geo<BN, NT>;
   constexpr int S = C::kStages;
+  constexpr int B = C::B;
+  constexpr int MT = C::MT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
   uint8_t* sX = smem + C::kOffX;
-  uint8_t* sX16 = smem + C::kOffX16;
   float* sRed = reinterpret_cast<float*>(smem + C::kOffRed);
   float4* sStat = reinterpret_cast<float4*>(smem + C::kOffStat);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kOffBar);  // TMA bytes of the stage landed
   uint64_t* empty_bar = full_bar + S;                                   // all consumer warps read the stage
-  uint64_t* xready_bar = empty_bar + S;                                 // fp16 activations of the stage written
   volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffFlag);
   volatile int* sLast = sAbort + 1;
-  volatile int* sInexact = sAbort + 2;  // [S]: an activation of the stage is outside the fp16 range
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
-  const int it_begin = static_cast<int>(split_start(cta, p.T, p.G));
-  const int it_end = static_cast<int>(split_start(cta + 1, p.T, p.G));
-  const int n_iter = it_end - it_begin;
-  const bool use_f16 = p.f16_path != 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kConsumerWarps);  // one arrival per consumer warp
-      mbar_init(&xready_bar[s], 1);              // the converter warp's lane 0
-      sInexact[s] = 0;
     }
     *sAbort = 0;
     *sLast = 0;
@@ -243,26 +299,39 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
   __syncthreads();
   pdl_launch_dependents();
 
+  StageIter it;
+  it.init(p, cta);
+  const int n_iter = it.n_iter;
+  // partial (stream-K) tiles of this CTA: the first and the last tile of its SK range, unless whole
+  const int sk_t0 = it.n_sk > 0 ? it.sk_begin / p.kiters : -1;
+  const int sk_t1 = it.n_sk > 0 ? (it.sk_end - 1) / p.kiters : -1;
+  const bool part0 = it.n_sk > 0 && !(sk_t0 * p.kiters >= it.sk_begin && (sk_t0 + 1) * p.kiters <= it.sk_end);
+  const bool part1 = it.n_sk > 0 && sk_t1 != sk_t0 &&
+                     !(sk_t1 * p.kiters >= it.sk_begin && (sk_t1 + 1) * p.kiters <= it.sk_end);
+
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ producer (one lane)
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
       const int npre = n_iter < S ? n_iter : S;
+      StageIter pi = it;
       for (int i = 0; i < npre; ++i) {  // weights do not depend on the previous kernel
-        const int gi = it_begin + i;
-        const int tile = gi / p.kiters;
-        const int kk = gi - tile * p.kiters;
         mbar_arrive_expect_tx(&full_bar[i], C::kTxBytes);
-        tma_load_2d(sW + i * kWStageBytes, &tmap_w, &full_bar[i], kk * kBK, tile * kBN, pol_w);
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          tma_load_2d(sW + i * kWStageBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[i], pi.kk * C::KS + b * 128,
+                      pi.tile * BN, pol_w);
+        pi.next(p);
       }
       pdl_wait();
+      StageIter xi = it;
       for (int i = 0; i < npre; ++i) {
-        const int gi = it_begin + i;
-        const int kk = gi % p.kiters;
         uint8_t* xs = sX + i * C::kXStageBytes;
-        tma_load_2d(xs, &tmap_x, &full_bar[i], kk * kBK, 0, pol_x);
-        tma_load_2d(xs + C::kXBoxBytes, &tmap_x, &full_bar[i], kk * kBK + 64, 0, pol_x);
+#pragma unroll
+        for (int b = 0; b < 2 * B; ++b)
+          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * C::KS + b * 64, 0, pol_x);
+        xi.next(p);
       }
       int issued = npre;
       for (int i = npre; i < n_iter; ++i) {
@@ -273,14 +342,16 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
           *sAbort = 1;
           break;
         }
-        const int gi = it_begin + i;
-        const int tile = gi / p.kiters;
-        const int kk = gi - tile * p.kiters;
         mbar_arrive_expect_tx(&full_bar[s], C::kTxBytes);
-        tma_load_2d(sW + s * kWStageBytes, &tmap_w, &full_bar[s], kk * kBK, tile * kBN, pol_w);
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          tma_load_2d(sW + s * kWStageBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[s], pi.kk * C::KS + b * 128,
+                      pi.tile * BN, pol_w);
         uint8_t* xs = sX + s * C::kXStageBytes;
-        tma_load_2d(xs, &tmap_x, &full_bar[s], kk * kBK, 0, pol_x);
-        tma_load_2d(xs + C::kXBoxBytes, &tmap_x, &full_bar[s], kk * kBK + 64, 0, pol_x);
+#pragma unroll
+        for (int b = 0; b < 2 * B; ++b)
+          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[s], pi.kk * C::KS + b * 64, 0, pol_x);
+        pi.next(p);
         issued = i + 1;
       }
       // Drain: every copy this CTA issued must land before shared memory is released.
@@ -298,77 +369,137 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     return;
   }
 
-  if (warp == kConverterWarp) {
-    // ------------------------------------------------------------------ activation converter (one warp)
-    // bf16 -> fp16 of each landed stage, 8-byte blocks per lane, same offsets in the fp16 buffer with pairs
-    // permuted to (k, k+2), (k+1, k+3); flags the stage if a value is outside the fp16 range.
-    if (!use_f16) return;
-    pdl_wait();
-    const uint32_t sX_u32 = smem_u32(sX), sX16_u32 = smem_u32(sX16);
-    for (int i = 0; i < n_iter; ++i) {
-      const int st = i % S;
-      if (!mbar_wait_bounded(&full_bar[st], static_cast<uint32_t>(i / S) & 1u, sAbort)) {
-        if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
-        *sAbort = 1;
-      }
-      uint32_t bad = 0;
-#pragma unroll
-      for (int j = 0; j < C::kXPairs / 32; ++j) {
-        const uint32_t off = static_cast<uint32_t>(st * C::kXStageBytes + (lane + 32 * j) * 8);
-        uint32_t w0, w1, o0, o1;
-        lds64(sX_u32 + off, w0, w1);
-        bad |= bf16x4_to_f16_pairs(w0, w1, o0, o1);
-        sts64(sX16_u32 + off, o0, o1);
-      }
-      const bool any_bad = __any_sync(0xffffffffu, bad != 0);
-      __syncwarp();
-      if (lane == 0) {
-        sInexact[st] = any_bad ? 1 : 0;
-        mbar_arrive(&xready_bar[st]);  // release: the warp's fp16 stores and the flag
-      }
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------------- consumers (16 warps)
-  pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
-  const int q = warp >> 1;   // m-tile group: rows [16*kJ*q, 16*kJ*(q + 1)) of the 128-row tile
-  const int h = warp & 1;    // which half of the 16-byte k chunks of each stage
-  const int g = lane >> 2;
-  const int t = lane & 3;
-  const int c = (t ^ h) | ((t & 1) << 2);  // this lane's 16-k chunk of each stage
-  const uint32_t sW_u32 = smem_u32(sW);
-  const uint32_t sX_u32 = smem_u32(sX);
-  const uint32_t sX16_u32 = smem_u32(sX16);
-  const uint32_t w_off = static_cast<uint32_t>((16 * kJ * q + g) * 128 + ((c ^ g) << 4));
-  const uint32_t x_off = static_cast<uint32_t>((c >> 2) * C::kXBoxBytes + g * 128);
-  const uint32_t x_u0 = static_cast<uint32_t>(((2 * (c & 3)) ^ g) << 4);
-  const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
-
   int* counters = reinterpret_cast<int*>(p.ws + kWsCounters);
   float* partials = reinterpret_cast<float*>(p.ws + kWsPartials);
   float4* tile_stats = reinterpret_cast<float4*>(p.ws + kWsStats);
-  const int first_tile = it_begin / p.kiters;
-  const int ctid = threadIdx.x;  // 0..511 among consumers
 
-  float acc[kJ][NT][4];
+  if (warp == kFixupWarp) {
+    // ------------------------------------------------------------------ fixup warp: stream-K partial tiles
+    pdl_wait();
+    for (int which = 0; which < 2; ++which) {
+      if (!(which == 0 ? part0 : part1)) continue;
+      const int tile = which == 0 ? sk_t0 : sk_t1;
+      named_bar_sync(which == 0 ? kBarFix0 : kBarFix1, kConsumerThreads + 32);  // this CTA's partial is written
+      const int it0 = tile * p.kiters;
+      const int c_first = cta_of(it0, p.Tsk, p.Gsk);
+      const int c_last = cta_of(min(it0 + p.kiters, p.Tsk) - 1, p.Tsk, p.Gsk);
+      int last = 0;
+      if (lane == 0) {
+        __threadfence();
+        last = atomicAdd(&counters[tile], 1) == c_last - c_first;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();
+      // Slot = [BN rows][8*NT tokens] fp32, read as float4: lane takes float4 f = lane + 32 j (row f / (2 NT),
+      // tokens 4 (lane % (2 NT)) + 0..3).  All of a contributor's loads (and those of U contributors) are issued
+      // before they are added, in ascending CTA order.
+      constexpr int F4 = BN * 2 * NT;
+      constexpr int PER = F4 / 32;
+      constexpr int PC = PER > 8 ? 8 : PER;   // float4 per lane per pass (bounded registers)
+      constexpr int U = PC >= 8 ? 1 : 8 / PC;  // contributors whose loads are in flight together
+      const int m_base = 4 * (lane % (2 * NT));
+      RowStat st[4];
 #pragma unroll
-  for (int j = 0; j < kJ; ++j)
+      for (int pass = 0; pass < PER / PC; ++pass) {
+        float4 v[PC];
+#pragma unroll
+        for (int j = 0; j < PC; ++j) v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int cc = c_first; cc <= c_last; cc += U) {
+          float4 a[U][PC];
+#pragma unroll
+          for (int uu = 0; uu < U; ++uu) {
+            if (cc + uu <= c_last) {
+              const int ft = static_cast<int>(split_start(cc + uu, p.Tsk, p.Gsk) / p.kiters);
+              const float4* sl = reinterpret_cast<const float4*>(
+                  partials + static_cast<size_t>(2 * (cc + uu) + (tile == ft ? 0 : 1)) * kPartialSlotFloats);
+#pragma unroll
+              for (int j = 0; j < PC; ++j) a[uu][j] = __ldcg(sl + lane + 32 * (pass * PC + j));
+            }
+          }
+#pragma unroll
+          for (int uu = 0; uu < U; ++uu) {
+            if (cc + uu <= c_last) {
+#pragma unroll
+              for (int j = 0; j < PC; ++j) {
+                v[j].x += a[uu][j].x;
+                v[j].y += a[uu][j].y;
+                v[j].z += a[uu][j].z;
+                v[j].w += a[uu][j].w;
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < PC; ++j) {
+          const int n = tile * BN + (lane + 32 * (pass * PC + j)) / (2 * NT);
+          const float sc = n < p.N ? __ldg(p.scale + n) : 0.f;
+          const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int m = m_base + e;
+            if constexpr (!HEAD) {
+              store_out(p, n, m, vv[e] * sc);
+            } else {
+              const __nv_bfloat16 rv = __float2bfloat16_rn(vv[e] * sc);
+              if (p.logits && m < p.M && n < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n] = rv;
+              const RowStat one =
+                  n < p.n_valid ? RowStat{__bfloat162float(rv), n, 1.f} : RowStat{-INFINITY, INT_MAX, 0.f};
+              st[e] = (pass == 0 && j == 0) ? one : stat_combine(st[e], one);
+            }
+          }
+        }
+      }
+      if constexpr (HEAD) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          RowStat s = st[e];
+#pragma unroll
+          for (int off = 2 * NT; off < 32; off <<= 1) s = stat_combine(s, stat_shfl_xor(s, off));
+          if (lane < 2 * NT)
+            tile_stats[static_cast<size_t>(tile) * 16 + m_base + e] = make_float4(s.m, __int_as_float(s.a), s.s, 0.f);
+        }
+        __threadfence();
+      }
+      if (lane == 0) counters[tile] = 0;  // ready for the next call on this workspace
+    }
+    if constexpr (HEAD) named_bar_sync(kBarEnd, kConsumerThreads + 32);
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers (8 warps)
+  pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
+  const int h = warp & 1;           // which half of each box's 16-byte k chunks
+  const int u = warp >> 1;          // unit: weight box b and pair of m-tiles mp
+  const int b = u % B;
+  const int mp = u / B;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  const int c = (t ^ h) | ((t & 1) << 2);  // this lane's 16-k chunk of the box
+  const uint32_t sW_u32 = smem_u32(sW);
+  const uint32_t sX_u32 = smem_u32(sX);
+  const uint32_t w_off = static_cast<uint32_t>(b * C::kWBoxBytes + (32 * mp + g) * 128 + ((c ^ g) << 4));
+  const uint32_t x_off = static_cast<uint32_t>((2 * b + (c >> 2)) * C::kXBoxBytes + g * 128);
+  const uint32_t x_u0 = static_cast<uint32_t>(((2 * (c & 3)) ^ g) << 4);
+  const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
+  const int ctid = threadIdx.x;  // 0..255 among consumers
+  const bool use_f16 = p.f16_path != 0;
+
+  float acc[2][NT][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[j][nt][e] = 0.f;
 
-  int tile = first_tile;
-  int kk = it_begin - first_tile * p.kiters;
   for (int i = 0; i < n_iter; ++i) {
     const int s = i % S;
-    if (!mbar_wait_bounded(use_f16 ? &xready_bar[s] : &full_bar[s], static_cast<uint32_t>(i / S) & 1u, sAbort)) {
+    if (!mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, sAbort)) {
       if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
       *sAbort = 1;
     }
-    const bool f16 = use_f16 && sInexact[s] == 0;
-    const uint32_t xbase = (f16 ? sX16_u32 : sX_u32) + s * C::kXStageBytes + x_off;
+    const uint32_t xbase = sX_u32 + s * C::kXStageBytes + x_off;
     uint4 xa[NT], xb[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -376,110 +507,93 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
       xb[nt] = lds128(xbase + nt * 1024 + x_u1);
     }
     const uint32_t wbase = sW_u32 + s * kWStageBytes + w_off;
-    uint4 ra[kJ], rb[kJ];
-#pragma unroll
-    for (int j = 0; j < kJ; ++j) {
-      ra[j] = lds128(wbase + j * 2048);
-      rb[j] = lds128(wbase + j * 2048 + 1024);
-    }
+    const uint4 ra0 = lds128(wbase), rb0 = lds128(wbase + 1024);
+    const uint4 ra1 = lds128(wbase + 2048), rb1 = lds128(wbase + 3072);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);  // release: this warp's reads of the slot are done
+
+    bool f16 = false;
+    uint4 xa16[NT], xb16[NT];
+    if (use_f16) {
+      uint32_t bad = 0;
 #pragma unroll
-    for (int j = 0; j < kJ; ++j) {
-      if (f16)
-        mma_chunk<NT, true>(acc[j], ra[j], rb[j], xa, xb);
-      else
-        mma_chunk<NT, false>(acc[j], ra[j], rb[j], xa, xb);
+      for (int nt = 0; nt < NT; ++nt) {
+        bad |= bf16x4_to_f16_pairs(xa[nt].x, xa[nt].y, xa16[nt].x, xa16[nt].y);
+        bad |= bf16x4_to_f16_pairs(xa[nt].z, xa[nt].w, xa16[nt].z, xa16[nt].w);
+        bad |= bf16x4_to_f16_pairs(xb[nt].x, xb[nt].y, xb16[nt].x, xb16[nt].y);
+        bad |= bf16x4_to_f16_pairs(xb[nt].z, xb[nt].w, xb16[nt].z, xb16[nt].w);
+      }
+      f16 = !__any_sync(0xffffffffu, bad != 0);
+    }
+    if (f16) {
+      mma_chunk<NT, true>(acc[0], ra0, rb0, xa16, xb16);
+      mma_chunk<NT, true>(acc[1], ra1, rb1, xa16, xb16);
+    } else {
+      mma_chunk<NT, false>(acc[0], ra0, rb0, xa, xb);
+      mma_chunk<NT, false>(acc[1], ra1, rb1, xa, xb);
     }
 
     // ------------------------------------------------------------ tile epilogue
-    const int cur_tile = tile;
-    const bool tile_end = (kk == p.kiters - 1) || (i == n_iter - 1);
-    if (++kk == p.kiters) {
-      kk = 0;
-      ++tile;
-    }
+    const int tile = it.tile;
+    const bool sk = it.sk;
+    const bool tile_end = (it.kk == p.kiters - 1) || (sk && i == it.n_sk - 1);
+    it.next(p);
     if (!tile_end) continue;
 
-    // fold the two k-halves held by warps (q, 0) and (q, 1): with one m-tile per warp, warp (q, 0) keeps it;
-    // with two, warp (q, h) keeps m-tile h of the group
-    float v[NT][4];
-    const int keep = kJ == 1 ? 0 : h;      // which of this warp's m-tiles it finishes
-    const bool owner = kJ == 1 ? (h == 0) : true;
+    // every warp dumps its two m-tile partials; warp w < MT then owns m-tile w
     {
-      float* mine = sRed + ((kJ == 1 ? q : warp) * 32 + lane) * 4 * NT;
-      if (kJ == 1 ? (h == 1) : true) {
+      float* mine = sRed + (warp * 2 * 32 + lane) * 4 * NT;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) mine[nt * 4 + e] = (kJ == 1 || keep == 1) ? acc[0][nt][e] : acc[kJ - 1][nt][e];
-      }
-      named_bar_sync(kBarPairBase + q, 64);
-      const float* other = kJ == 1 ? mine : sRed + ((warp ^ 1) * 32 + lane) * 4 * NT;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[nt][e] = (keep == 0 ? acc[0][nt][e] : acc[kJ - 1][nt][e]) + other[nt * 4 + e];
-      named_bar_sync(kBarPairBase + q, 64);
+          for (int e = 0; e < 4; ++e) {
+            mine[j * 32 * 4 * NT + nt * 4 + e] = acc[j][nt][e];
+            acc[j][nt][e] = 0.f;
+          }
     }
-#pragma unroll
-    for (int j = 0; j < kJ; ++j)
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    float v[NT][4];
+    const bool owner = warp < MT;
+    if (owner) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][nt][e] = 0.f;
-
-    const int mt = kJ * q + keep;  // m-tile finished by this warp (if owner)
-    const int rl0 = 16 * mt + g;   // local rows rl0 and rl0 + 8
-    const int tile_it0 = cur_tile * p.kiters;
-    const bool whole = (tile_it0 >= it_begin) && (tile_it0 + p.kiters <= it_end);
-    bool finish = whole;
+        for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
+#pragma unroll
+      for (int bb = 0; bb < B; ++bb)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int src = 2 * ((warp >> 1) * B + bb) + hh;
+          const float* o = sRed + ((src * 2 + (warp & 1)) * 32 + lane) * 4 * NT;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[nt][e] += o[nt * 4 + e];
+        }
+    }
+    const int rl0 = 16 * warp + g;  // owner's rows rl0 and rl0 + 8 of the tile
+    const int tile_it0 = tile * p.kiters;
+    const bool whole = !sk || (tile_it0 >= it.sk_begin && tile_it0 + p.kiters <= it.sk_end);
     if (!whole) {
+      // stream-K partial: store it and hand the reduction to the fixup warp
       if (owner) {
-        const int which = (cur_tile == first_tile) ? 0 : 1;
+        const int which = (tile == sk_t0) ? 0 : 1;
         float* slot = partials + static_cast<size_t>(2 * cta + which) * kPartialSlotFloats;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
+        for (int nt = 0; nt < NT; ++nt) {  // [BN rows][8*NT tokens]
           const int col = 8 * nt + 2 * t;
-          *reinterpret_cast<float2*>(slot + rl0 * 16 + col) = make_float2(v[nt][0], v[nt][1]);
-          *reinterpret_cast<float2*>(slot + (rl0 + 8) * 16 + col) = make_float2(v[nt][2], v[nt][3]);
+          *reinterpret_cast<float2*>(slot + rl0 * 8 * NT + col) = make_float2(v[nt][0], v[nt][1]);
+          *reinterpret_cast<float2*>(slot + (rl0 + 8) * 8 * NT + col) = make_float2(v[nt][2], v[nt][3]);
         }
-        __threadfence();
       }
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (ctid == 0) {
-        const int c_first = cta_of(tile_it0, p.T, p.G);
-        const int c_last = cta_of(min(tile_it0 + p.kiters, p.T) - 1, p.T, p.G);
-        const int old = atomicAdd(&counters[cur_tile], 1);
-        *sLast = (old == c_last - c_first) ? 1 : 0;
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      finish = *sLast != 0;
-      if (finish && owner) {
-        __threadfence();
-        const int c_first = cta_of(tile_it0, p.T, p.G);
-        const int c_last = cta_of(min(tile_it0 + p.kiters, p.T) - 1, p.T, p.G);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
-        for (int cc = c_first; cc <= c_last; ++cc) {
-          const int ft = static_cast<int>(split_start(cc, p.T, p.G) / p.kiters);
-          const float* sl = partials + static_cast<size_t>(2 * cc + (cur_tile == ft ? 0 : 1)) * kPartialSlotFloats;
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const int col = 8 * nt + 2 * t;
-            const float2 a = __ldcg(reinterpret_cast<const float2*>(sl + rl0 * 16 + col));
-            const float2 b = __ldcg(reinterpret_cast<const float2*>(sl + (rl0 + 8) * 16 + col));
-            v[nt][0] += a.x; v[nt][1] += a.y; v[nt][2] += b.x; v[nt][3] += b.y;
-          }
-        }
-        if (ctid == 0) counters[cur_tile] = 0;  // ready for the next call on this workspace
-      }
+      named_bar_sync(kBarConsumers, kConsumerThreads);  // sRed reads done before the next tile's dump
+      named_bar_arrive(tile == sk_t0 ? kBarFix0 : kBarFix1, kConsumerThreads + 32);
+      continue;
     }
-    if (!finish) continue;
 
-    const int n0 = cur_tile * kBN + rl0;
+    const int n0 = tile * BN + rl0;
     const int n1 = n0 + 8;
     if constexpr (!HEAD) {
       if (owner) {
@@ -494,77 +608,74 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
           store_out(p, n1, m0 + 1, v[nt][3] * s1);
         }
       }
+      named_bar_sync(kBarConsumers, kConsumerThreads);  // sRed reads done before the next tile's dump
     } else {
-      // bf16 logits, then per-token statistics of this tile over the same bf16 values
       if (owner) {
         const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
         const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-          for (int b = 0; b < 2; ++b) {
-            const int m = 8 * nt + 2 * t + b;
-            const __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][b] * s0);
-            const __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + b] * s1);
+          for (int bq = 0; bq < 2; ++bq) {
+            const int m = 8 * nt + 2 * t + bq;
+            const __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][bq] * s0);
+            const __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + bq] * s1);
             if (p.logits && m < p.M) {
               if (n0 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n0] = r0;
               if (n1 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n1] = r1;
             }
-            RowStat st{-INFINITY, INT_MAX, 0.f};
-            if (n0 < p.n_valid) st = RowStat{__bfloat162float(r0), n0, 1.f};
-            if (n1 < p.n_valid) st = stat_combine(st, RowStat{__bfloat162float(r1), n1, 1.f});
-            st = stat_combine(st, stat_shfl_xor(st, 4));
-            st = stat_combine(st, stat_shfl_xor(st, 8));
-            st = stat_combine(st, stat_shfl_xor(st, 16));
-            if (g == 0) sStat[mt * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
+            const RowStat st = warp_tile_stat(p, n0, n1, r0, r1);
+            if (g == 0) sStat[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
           }
         }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (warp == 0) {
-        if (lane < 8 * NT) {
-          RowStat st{-INFINITY, INT_MAX, 0.f};
-          for (int w = 0; w < kMTiles; ++w) {
-            const float4 f = sStat[w * 16 + lane];
-            st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
-          }
-          tile_stats[static_cast<size_t>(cur_tile) * 16 + lane] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
-          __threadfence();
+      if (warp == 0 && lane < 8 * NT) {
+        RowStat st{-INFINITY, INT_MAX, 0.f};
+        for (int w = 0; w < MT; ++w) {
+          const float4 f = sStat[w * 16 + lane];
+          st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
         }
-        __syncwarp();
-        if (lane == 0) {
-          const unsigned old = atomicAdd(reinterpret_cast<unsigned*>(p.ws) + 1, 1u);
-          *sLast = (old == static_cast<unsigned>(p.ntiles - 1)) ? 1 : 0;
-        }
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (*sLast) {
-        // the last finished tile folds all tiles (fixed order: strided per thread, then a fixed tree)
+        tile_stats[static_cast<size_t>(tile) * 16 + lane] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
         __threadfence();
-        for (int m = 0; m < p.M; ++m) {
-          RowStat st{-INFINITY, INT_MAX, 0.f};
-          for (int j = ctid; j < p.ntiles; j += kConsumerThreads) {
-            const float4 f = __ldcg(tile_stats + static_cast<size_t>(j) * 16 + m);
-            st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
-          }
-#pragma unroll
-          for (int off = 1; off < 32; off <<= 1) st = stat_combine(st, stat_shfl_xor(st, off));
-          if (lane == 0) reinterpret_cast<float4*>(sRed)[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
-        }
-        named_bar_sync(kBarConsumers, kConsumerThreads);
-        if (warp == 0 && lane < p.M) {
-          RowStat st{-INFINITY, INT_MAX, 0.f};
-          for (int w = 0; w < kConsumerWarps; ++w) {
-            const float4 f = reinterpret_cast<const float4*>(sRed)[w * 16 + lane];
-            st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
-          }
-          p.row_max[lane] = st.m;
-          p.row_argmax[lane] = static_cast<long long>(st.a) + p.vocab_offset;
-          p.row_lse[lane] = st.m + logf(st.s);
-        }
-        if (ctid == 0) reinterpret_cast<unsigned*>(p.ws)[1] = 0u;
       }
-      named_bar_sync(kBarConsumers, kConsumerThreads);  // sStat / sRed / sLast reuse by the next tile
+      named_bar_sync(kBarConsumers, kConsumerThreads);  // sRed / sStat reuse by the next tile
+    }
+  }
+
+  if constexpr (HEAD) {
+    // the CTA that finishes last folds the per-tile statistics of all tiles (fixed order)
+    named_bar_sync(kBarEnd, kConsumerThreads + 32);
+    if (ctid == 0) {
+      __threadfence();
+      const unsigned old = atomicAdd(reinterpret_cast<unsigned*>(p.ws) + 2, 1u);
+      *sLast = (old == static_cast<unsigned>(p.G - 1)) ? 1 : 0;
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (*sLast) {
+      __threadfence();
+      for (int m = 0; m < p.M; ++m) {
+        RowStat st{-INFINITY, INT_MAX, 0.f};
+        for (int j = ctid; j < p.ntiles; j += kConsumerThreads) {
+          const float4 f = __ldcg(tile_stats + static_cast<size_t>(j) * 16 + m);
+          st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
+        }
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) st = stat_combine(st, stat_shfl_xor(st, off));
+        if (lane == 0) sStat[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
+      }
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      if (warp == 0 && lane < p.M) {
+        RowStat st{-INFINITY, INT_MAX, 0.f};
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float4 f = sStat[w * 16 + lane];
+          st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
+        }
+        p.row_max[lane] = st.m;
+        p.row_argmax[lane] = static_cast<long long>(st.a) + p.vocab_offset;
+        p.row_lse[lane] = st.m + logf(st.s);
+      }
+      if (ctid == 0) reinterpret_cast<unsigned*>(p.ws)[2] = 0u;
     }
   }
 }
@@ -589,9 +700,9 @@ int fail(int code, const std::string& msg) {
 }
 
 struct DeviceInfo {
-  int ok = 0;          // 1 = checked and sm_100, -1 = wrong arch
+  int ok = 0;             // 1 = checked and sm_100, -1 = wrong arch
   int sm_count = 0;
-  unsigned smem_set = 0;  // bit per kernel instance with the dynamic smem attribute set
+  unsigned smem_set = 0;  // bit per kernel instance with the dynamic shared memory attribute set
 };
 std::mutex g_mu;
 DeviceInfo g_dev[64];
@@ -612,7 +723,8 @@ int device_info(int* dev_out, DeviceInfo** info_out) {
     d.ok = (major == 10 && minor == 0) ? 1 : -1;
     d.sm_count = sms;
   }
-  if (d.ok != 1) return fail(QF_ERR_ARCH, "libqf_b200 is built for sm_100a (B200); this device is not compute capability 10.0");
+  if (d.ok != 1)
+    return fail(QF_ERR_ARCH, "libqf_b200 is built for sm_100a (B200); this device is not compute capability 10.0");
   if (!g_encode) {
     cudaDriverEntryPointQueryResult qres;
     void* fn = nullptr;
@@ -626,8 +738,7 @@ int device_info(int* dev_out, DeviceInfo** info_out) {
   return QF_OK;
 }
 
-// Optional upper bound on the stream-K grid (environment QF_GRID_CAP, read once): lets tests exercise other
-// split patterns, e.g. one CTA per whole problem.
+// Optional upper bound on the grid (environment QF_GRID_CAP, read once): lets tests exercise other schedules.
 int grid_cap() {
   static const int cap = [] {
     const char* v = std::getenv("QF_GRID_CAP");
@@ -636,8 +747,8 @@ int grid_cap() {
   return cap;
 }
 
-// Activation path (environment QF_F16_PATH, read once): 1 (default) converts each stage's activations to
-// fp16 for the cheaper exact weight conversion; 0 keeps every stage on the bf16 path.
+// Activation path (environment QF_F16_PATH, read once): 1 (default) converts activations to fp16 for the cheaper
+// exact weight conversion (warps fall back to bf16 where activations leave the fp16 range); 0 keeps bf16.
 int f16_path() {
   static const int v = [] {
     const char* e = std::getenv("QF_F16_PATH");
@@ -646,26 +757,33 @@ int f16_path() {
   return v;
 }
 
-int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner,
-              uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+              uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
   cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  (void)elem_bytes;
   CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(QF_ERR_DRIVER, "cuTensorMapEncodeTiled rejected the tensor (error " + std::to_string(r) + ")");
+  if (r != CUDA_SUCCESS)
+    return fail(QF_ERR_DRIVER, "cuTensorMapEncodeTiled rejected the tensor (error " + std::to_string(r) + ")");
   return QF_OK;
 }
 
-template <int NT, bool HEAD>
-int launch_streamk(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo,
-                   unsigned flags, cudaStream_t stream) {
-  using C = Cfg<NT>;
-  auto kern = w8a16_streamk_kernel<NT, HEAD>;
-  const unsigned bit = 1u << ((NT - 1) * 2 + (HEAD ? 1 : 0));
+// Tile height: the widest of 128 / 64 / 32 rows that still gives every SM a whole tile.
+int pick_bn(int N, int sms) {
+  if ((N + 127) / 128 >= sms) return 128;
+  if ((N + 63) / 64 >= sms) return 64;
+  return 32;
+}
+
+template <int BN, int NT, bool HEAD>
+int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, unsigned flags,
+           cudaStream_t stream) {
+  using C = Geo<BN, NT>;
+  auto kern = w8a16_kernel<BN, NT, HEAD>;
+  const unsigned bit = 1u << ((BN == 128 ? 0 : BN == 64 ? 1 : 2) * 4 + (NT - 1) * 2 + (HEAD ? 1 : 0));
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!(dinfo->smem_set & bit)) {
@@ -675,26 +793,35 @@ int launch_streamk(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Par
     }
   }
   CUtensorMap tw, tx;
-  int rc = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
-                     static_cast<uint64_t>(ldw), kBK, kBN);
+  int rc = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
+                     static_cast<uint64_t>(ldw), 128, BN);
   if (rc) return rc;
   const uint64_t xstride = (p.M > 1) ? static_cast<uint64_t>(ldx) * 2 : (static_cast<uint64_t>(p.K) * 2 + 15) / 16 * 16;
-  rc = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M),
+  rc = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M),
                  xstride, 64, 8 * NT);
   if (rc) return rc;
 
   p.f16_path = f16_path();
-  p.kiters = (p.K + kBK - 1) / kBK;
-  p.ntiles = (p.N + kBN - 1) / kBN;
-  p.T = p.kiters * p.ntiles;
+  p.kiters = (p.K + C::KS - 1) / C::KS;
+  p.ntiles = (p.N + BN - 1) / BN;
+  const long long total = static_cast<long long>(p.kiters) * p.ntiles;
   int G = dinfo->sm_count;
   if (G > kMaxGrid) G = kMaxGrid;
   if (grid_cap() > 0 && G > grid_cap()) G = grid_cap();
-  if (G > p.T) G = p.T;
+  if (G > total) G = static_cast<int>(total);
   p.G = G;
+  p.q = p.ntiles / G;
+  p.r = p.ntiles - p.q * G;
+  p.Tsk = p.r * p.kiters;
+  // At most about kMaxSplit CTAs share a stream-K tile: fewer, longer shares keep the fixup short (it reads every
+  // contributor's partial) at a small cost in balance.
+  long long gsk = p.Tsk < G ? p.Tsk : G;
+  if (gsk > static_cast<long long>(kMaxSplit) * p.r) gsk = static_cast<long long>(kMaxSplit) * p.r;
+  p.Gsk = static_cast<int>(gsk);
+  if (p.q == 0) p.G = p.Gsk;  // all work is stream-K: CTAs without a share are not launched
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(G);
+  cfg.gridDim = dim3(p.G);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
@@ -706,6 +833,20 @@ int launch_streamk(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Par
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
   if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("launch: ") + cudaGetErrorString(e));
   return QF_OK;
+}
+
+template <bool HEAD>
+int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo,
+               unsigned flags, cudaStream_t st) {
+  const int bn = pick_bn(p.N, dinfo->sm_count);
+  if (p.M <= 8) {
+    if (bn == 128) return launch<128, 1, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
+    if (bn == 64) return launch<64, 1, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
+    return launch<32, 1, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
+  }
+  if (bn == 128) return launch<128, 2, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
+  if (bn == 64) return launch<64, 2, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
+  return launch<32, 2, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
 }
 
 int check_common(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, int M, int N, int K,
@@ -738,7 +879,8 @@ extern "C" {
 size_t qf_w8a16_workspace_bytes(int M, int N, int K) {
   (void)M;
   (void)K;
-  const size_t ntiles = N > 0 ? (static_cast<size_t>(N) + kBN - 1) / kBN : 0;
+  // head statistics: 16 float4 per tile, sized for the narrowest tiles (32 rows)
+  const size_t ntiles = N > 0 ? (static_cast<size_t>(N) + 31) / 32 : 0;
   return kWsStats + ntiles * 16 * sizeof(float4);
 }
 
@@ -772,8 +914,7 @@ int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
-  if (M <= 8) return launch_streamk<1, false>(x, ldx, w, ldw, p, dinfo, flags, st);
-  return launch_streamk<2, false>(x, ldx, w, ldw, p, dinfo, flags, st);
+  return launch_any<false>(x, ldx, w, ldw, p, dinfo, flags, st);
 }
 
 int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* logits,
@@ -803,9 +944,7 @@ int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
   p.row_max = row_max;
   p.row_argmax = reinterpret_cast<long long*>(row_argmax);
   p.row_lse = row_lse;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (M <= 8) return launch_streamk<1, true>(x, ldx, w, ldw, p, dinfo, flags, st);
-  return launch_streamk<2, true>(x, ldx, w, ldw, p, dinfo, flags, st);
+  return launch_any<true>(x, ldx, w, ldw, p, dinfo, flags, static_cast<cudaStream_t>(stream));
 }
 
 int qf_workspace_status(void* ws, void* stream, int* status) {
@@ -844,11 +983,11 @@ int qf_abi_version(void) { return QF_ABI_VERSION; }
 }  // extern "C"
 
 // ================================================================================== allocation-free entry
-// qf_w8a16_gemm_noalloc: the same stream-K GEMM with its scratch (split-tile counters and fp32 partial tiles)
-// in a fixed array of this library instead of a caller-provided workspace, for callers that cannot allocate
-// device memory themselves (a host that embeds only this library and has no device allocator, e.g. a Go or
-// Java binding over the C ABI, or a latency-critical path that must not call cudaMalloc, which can
-// synchronise the device).  The array lives in every GPU that loads the library until the process exits.
+// qf_w8a16_gemm_noalloc: the same GEMM with its scratch (split-tile counters and fp32 partial tiles) in a fixed
+// array of this library instead of a caller-provided workspace, for callers that cannot allocate device memory
+// themselves (a host that embeds only this library and has no device allocator, e.g. a Go or Java binding over
+// the C ABI, or a latency-critical path that must not call cudaMalloc, which can synchronise the device).  The
+// array lives in every GPU that loads the library until the process exits.
 namespace qf {
 namespace {
 
@@ -868,7 +1007,8 @@ int noalloc_scratch(int dev, void** out) {
   if (!g_noalloc_ptr[dev]) {
     void* ptr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || !ptr) return fail(QF_ERR_LAUNCH, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    if (e != cudaSuccess || !ptr)
+      return fail(QF_ERR_LAUNCH, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
     g_noalloc_ptr[dev] = ptr;
   }
   *out = g_noalloc_ptr[dev];
@@ -909,9 +1049,9 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
   rc = noalloc_scratch(dev, &scratch);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The array keeps the previous call's contents: clear the error word and this call's tile counters.
-  const size_t ntiles = (static_cast<size_t>(N) + kBN - 1) / kBN;
-  cudaError_t e = cudaMemsetAsync(scratch, 0, kWsCounters + sizeof(int) * ntiles, st);
+  // The array keeps the previous call's contents: clear the header and the tile counters this call can use.
+  const size_t ntiles = (static_cast<size_t>(N) + 31) / 32;
+  cudaError_t e = cudaMemsetAsync(scratch, 0, kWsCounters + sizeof(int) * (ntiles < kMaxTiles ? ntiles : kMaxTiles), st);
   if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   Params p = {};
   p.scale = scale;
@@ -929,6 +1069,5 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
     e = cudaGetLastError();
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
-  if (M <= 8) return launch_streamk<1, false>(x, ldx, w, ldw, p, dinfo, flags, st);
-  return launch_streamk<2, false>(x, ldx, w, ldw, p, dinfo, flags, st);
+  return launch_any<false>(x, ldx, w, ldw, p, dinfo, flags, st);
 }

@@ -1,0 +1,42 @@
+"""Run as ``python -m tests._grid_cap_case`` with QF_GRID_CAP set: GEMM and head shapes whose tiles are split
+between CTAs in ways the full grid never produces (one CTA, a few CTAs, stream-K shares of many stages),
+checked against the oracle.  Exits non-zero on a mismatch.  Used by test_gpu_schedule.py."""
+from __future__ import annotations
+
+import sys
+
+import numpy as np
+
+
+def main() -> int:
+    import torch
+    from oracle import w8a16_oracle as orc
+    from qwen_a100_fastpath_b200.w8a16 import pick_config, w8a16_head, w8a16_mm
+    from tests.conftest import from_dev_bf16, to_dev_bf16
+    from tests.test_gpu_gemm import bf16_close
+    dev = torch.device("cuda", 0)
+    for (N, K, M) in [(1000, 1024, 5), (10240, 1024, 3), (4100, 2048, 12), (19072, 512, 1)]:
+        x, W, s = orc.make_inputs(N + K + M, M, N, K)
+        y = w8a16_mm(to_dev_bf16(x, dev), torch.from_numpy(W).to(dev).t(), torch.from_numpy(s).to(dev),
+                     pick_config(N, K), torch.bfloat16)
+        torch.cuda.synchronize()
+        bf16_close(from_dev_bf16(y), orc.w8a16_mm(x, W, s, "bf16"))
+    for (V, H, M, pad) in [(4100, 2048, 4, 36), (16384 + 640, 1024, 16, 64)]:
+        x, W, s = orc.make_inputs(V + H, M, V, H)
+        logits, mx, am, lse = w8a16_head(to_dev_bf16(x, dev), torch.from_numpy(W).to(dev).t(),
+                                         torch.from_numpy(s).to(dev), n_valid=V - pad, vocab_offset=0)
+        torch.cuda.synchronize()
+        lg = from_dev_bf16(logits)
+        assert np.mean(lg != orc.w8a16_mm(x, W, s, "bf16")) < 0.01
+        mx_own, am_own, lse_own = orc.head_stats(lg, V - pad, 0)
+        assert np.array_equal(mx.cpu().numpy(), mx_own)
+        assert np.array_equal(am.cpu().numpy(), am_own)
+        np.testing.assert_allclose(lse.cpu().numpy(), lse_own, rtol=2e-6)
+    from qwen_a100_fastpath_b200.w8a16 import workspace_status
+    assert workspace_status() == 0
+    print("ok")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

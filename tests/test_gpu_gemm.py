@@ -72,6 +72,9 @@ SHAPES = [
     (384, 1000, 16, 1008, 1008),
     (1, 4096, 7, None, None),          # single output channel
     (4352, 128, 4, None, None),        # one k stage per tile
+    (19072, 1024, 5, None, None),      # 149 tiles of 128 rows: one stream-K tile shared by 8 CTAs
+    (37984, 512, 12, None, None),      # two token tiles, 2 whole tiles per CTA + 1 stream-K tile
+    (17024, 256, 3, None, None),       # 64-row tiles
 ]
 
 
