@@ -56,7 +56,6 @@ constexpr int kProducerWarp = 8;            // TMA issue (one lane)
 constexpr int kFixupWarp = 9;               // reduction of stream-K partial tiles
 constexpr int kThreads = 10 * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kWStageBytes = 16384;         // weight bytes per pipeline stage
 constexpr int kMaxBN = 128;
 constexpr int kMaxGrid = 256;
 constexpr int kMaxTiles = QF_MAX_N / kMaxBN;  // tile counters (tiles narrower than 128 rows only when N < 64*SMs)
@@ -75,29 +74,30 @@ constexpr size_t kWsPartials = (kWsZeroBytes + 1023) / 1024 * 1024;
 constexpr size_t kPartialSlotFloats = kMaxBN * 16;              // [BN rows][8*NT tokens]
 constexpr size_t kWsStats = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kMaxGrid;
 
-template <int BN, int NT> struct Geo {
-  static constexpr int KS = kWStageBytes / BN;                  // k bytes per stage: 128, 256, 512
+template <int BN, int NT, int KS> struct Geo {
   static constexpr int B = KS / 128;                            // 128-byte weight boxes per stage
   static constexpr int MT = BN / 16;                            // m-tiles per tile (8, 4, 2)
+  static constexpr int NMP = MT / 2;                            // m-tile pairs (one per consumer warp pair)
+  static constexpr int BPW = B * NMP / 4;                       // weight boxes per consumer warp per stage
   static constexpr int kWBoxBytes = BN * 128;
-  static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT tokens][64 bf16]
+  static constexpr int kWBytes = BN * KS;                       // weight bytes per stage
+  static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT tokens][64 bf16] (rows >= M stay zero)
   static constexpr int kXStageBytes = 2 * B * kXBoxBytes;
-  static constexpr int kStageBytes = kWStageBytes + kXStageBytes;
+  static constexpr int kStageBytes = kWBytes + kXStageBytes;
   static constexpr int kRedBytes = kConsumerWarps * 2 * 32 * 4 * NT * 4;  // [warp][m-tile of pair][lane][4NT]
   static constexpr int kStatBytes = 8 * 16 * 16;                          // float4 [m-tile][token]
   static constexpr int kFixedBytes = kRedBytes + kStatBytes + 2 * 16 * 8 + 64 + 1024;
   static constexpr int kBudget = 226 * 1024;
   static constexpr int kStagesFit = (kBudget - kFixedBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 10 ? 10 : kStagesFit;
-  static constexpr int kOffX = kStages * kWStageBytes;
+  static constexpr int kOffX = kStages * kWBytes;
   static constexpr int kOffRed = kOffX + kStages * kXStageBytes;
   static constexpr int kOffStat = kOffRed + kRedBytes;
   static constexpr int kOffBar = kOffStat + kStatBytes;       // full[S], empty[S]
   static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;  // abort, last
   static constexpr int kSmemBytes = kOffFlag + 64 + 1024;     // + alignment slack
-  static constexpr uint32_t kTxBytes = kStageBytes;
-  static_assert(MT / 2 * B == kConsumerWarps / 2, "eight warps cover the stage");
-  static_assert(kStages >= 4, "pipeline too shallow");
+  static_assert(BPW >= 1 && B * NMP == 4 * BPW, "the four warp pairs cover the stage's boxes evenly");
+  static_assert(kStages >= 3, "pipeline too shallow");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -115,6 +115,7 @@ struct Params {
   int Gsk;
   uint8_t* ws;
   int f16_path;
+  uint32_t x_tx;  // activation bytes per stage: 2 B boxes of M rows x 128 bytes
   // head
   __nv_bfloat16* logits;
   int64_t ldl;
@@ -185,6 +186,7 @@ __device__ __forceinline__ void store_out(const Params& p, int n, int m, float v
   }
 }
 
+// Walks a CTA's stages in order: its stream-K share of tiles 0..r-1, then its whole tiles.
 // Walks a CTA's stages in order: its stream-K share of tiles 0..r-1, then its whole tiles.
 struct StageIter {
   int tile, kk, i;
@@ -264,14 +266,15 @@ __device__ __forceinline__ RowStat warp_tile_stat(const Params& p, int n0, int n
   return st;
 }
 
-template <int BN, int NT, bool HEAD>
+template <int BN, int NT, int KS, bool HEAD>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  const Params p) {
-  using C = Geo<BN, NT>;
+  using C = Geo<BN, NT, KS>;
   constexpr int S = C::kStages;
   constexpr int B = C::B;
   constexpr int MT = C::MT;
+  constexpr int NMP = C::NMP;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -296,6 +299,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     *sLast = 0;
     fence_mbar_init();
   }
+  {
+    // Token rows M .. 8*NT-1 of every activation box are never written by the copies (the boxes are M rows high):
+    // zero them once so that those MMA columns compute zeros.
+    const int zrows = 8 * NT - p.M;
+    const int per_box = zrows * 8;  // 16-byte units
+    for (int idx = threadIdx.x; idx < S * 2 * B * per_box; idx += kThreads) {
+      const int box = idx / per_box;
+      const int rem = idx - box * per_box;
+      *reinterpret_cast<uint4*>(sX + box * C::kXBoxBytes + (p.M + rem / 8) * 128 + (rem % 8) * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
   __syncthreads();
   pdl_launch_dependents();
 
@@ -317,10 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int npre = n_iter < S ? n_iter : S;
       StageIter pi = it;
       for (int i = 0; i < npre; ++i) {  // weights do not depend on the previous kernel
-        mbar_arrive_expect_tx(&full_bar[i], C::kTxBytes);
+        mbar_arrive_expect_tx(&full_bar[i], C::kWBytes + p.x_tx);
 #pragma unroll
         for (int b = 0; b < B; ++b)
-          tma_load_2d(sW + i * kWStageBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[i], pi.kk * C::KS + b * 128,
+          tma_load_2d(sW + i * C::kWBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[i], pi.kk * KS + b * 128,
                       pi.tile * BN, pol_w);
         pi.next(p);
       }
@@ -330,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* xs = sX + i * C::kXStageBytes;
 #pragma unroll
         for (int b = 0; b < 2 * B; ++b)
-          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * C::KS + b * 64, 0, pol_x);
+          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * KS + b * 64, 0, pol_x);
         xi.next(p);
       }
       int issued = npre;
@@ -342,15 +357,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           *sAbort = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full_bar[s], C::kTxBytes);
+        mbar_arrive_expect_tx(&full_bar[s], C::kWBytes + p.x_tx);
 #pragma unroll
         for (int b = 0; b < B; ++b)
-          tma_load_2d(sW + s * kWStageBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[s], pi.kk * C::KS + b * 128,
+          tma_load_2d(sW + s * C::kWBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[s], pi.kk * KS + b * 128,
                       pi.tile * BN, pol_w);
         uint8_t* xs = sX + s * C::kXStageBytes;
 #pragma unroll
         for (int b = 0; b < 2 * B; ++b)
-          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[s], pi.kk * C::KS + b * 64, 0, pol_x);
+          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[s], pi.kk * KS + b * 64, 0, pol_x);
         pi.next(p);
         issued = i + 1;
       }
@@ -469,17 +484,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // -------------------------------------------------------------------- consumers (8 warps)
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
+  // Warp (u, h), u = warp / 2: m-tile pair mp = u % NMP, weight boxes b = u / NMP + j * (4 / NMP), j < BPW.
   const int h = warp & 1;           // which half of each box's 16-byte k chunks
-  const int u = warp >> 1;          // unit: weight box b and pair of m-tiles mp
-  const int b = u % B;
-  const int mp = u / B;
+  const int u = warp >> 1;
+  const int mp = u % NMP;
+  const int b0 = u / NMP;
   const int g = lane >> 2;
   const int t = lane & 3;
   const int c = (t ^ h) | ((t & 1) << 2);  // this lane's 16-k chunk of the box
   const uint32_t sW_u32 = smem_u32(sW);
   const uint32_t sX_u32 = smem_u32(sX);
-  const uint32_t w_off = static_cast<uint32_t>(b * C::kWBoxBytes + (32 * mp + g) * 128 + ((c ^ g) << 4));
-  const uint32_t x_off = static_cast<uint32_t>((2 * b + (c >> 2)) * C::kXBoxBytes + g * 128);
+  const uint32_t w_off = static_cast<uint32_t>(b0 * C::kWBoxBytes + (32 * mp + g) * 128 + ((c ^ g) << 4));
+  const uint32_t x_off = static_cast<uint32_t>((2 * b0 + (c >> 2)) * C::kXBoxBytes + g * 128);
   const uint32_t x_u0 = static_cast<uint32_t>(((2 * (c & 3)) ^ g) << 4);
   const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
   const int ctid = threadIdx.x;  // 0..255 among consumers
@@ -499,38 +515,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
       *sAbort = 1;
     }
-    const uint32_t xbase = sX_u32 + s * C::kXStageBytes + x_off;
-    uint4 xa[NT], xb[NT];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      xa[nt] = lds128(xbase + nt * 1024 + x_u0);
-      xb[nt] = lds128(xbase + nt * 1024 + x_u1);
-    }
-    const uint32_t wbase = sW_u32 + s * kWStageBytes + w_off;
-    const uint4 ra0 = lds128(wbase), rb0 = lds128(wbase + 1024);
-    const uint4 ra1 = lds128(wbase + 2048), rb1 = lds128(wbase + 3072);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);  // release: this warp's reads of the slot are done
-
-    bool f16 = false;
-    uint4 xa16[NT], xb16[NT];
-    if (use_f16) {
-      uint32_t bad = 0;
+    for (int jb = 0; jb < C::BPW; ++jb) {
+      const int db = jb * (4 / NMP);  // box offset from b0
+      const uint32_t xbase = sX_u32 + s * C::kXStageBytes + x_off + 2 * db * C::kXBoxBytes;
+      uint4 xa[NT], xb[NT];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        bad |= bf16x4_to_f16_pairs(xa[nt].x, xa[nt].y, xa16[nt].x, xa16[nt].y);
-        bad |= bf16x4_to_f16_pairs(xa[nt].z, xa[nt].w, xa16[nt].z, xa16[nt].w);
-        bad |= bf16x4_to_f16_pairs(xb[nt].x, xb[nt].y, xb16[nt].x, xb16[nt].y);
-        bad |= bf16x4_to_f16_pairs(xb[nt].z, xb[nt].w, xb16[nt].z, xb16[nt].w);
+        xa[nt] = lds128(xbase + nt * 1024 + x_u0);
+        xb[nt] = lds128(xbase + nt * 1024 + x_u1);
       }
-      f16 = !__any_sync(0xffffffffu, bad != 0);
-    }
-    if (f16) {
-      mma_chunk<NT, true>(acc[0], ra0, rb0, xa16, xb16);
-      mma_chunk<NT, true>(acc[1], ra1, rb1, xa16, xb16);
-    } else {
-      mma_chunk<NT, false>(acc[0], ra0, rb0, xa, xb);
-      mma_chunk<NT, false>(acc[1], ra1, rb1, xa, xb);
+      const uint32_t wbase = sW_u32 + s * C::kWBytes + w_off + db * C::kWBoxBytes;
+      const uint4 ra0 = lds128(wbase), rb0 = lds128(wbase + 1024);
+      const uint4 ra1 = lds128(wbase + 2048), rb1 = lds128(wbase + 3072);
+      if (jb == C::BPW - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);  // release: this warp's reads of the slot are done
+      }
+
+      bool f16 = false;
+      uint4 xa16[NT], xb16[NT];
+      if (use_f16) {
+        uint32_t bad = 0;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          bad |= bf16x4_to_f16_pairs(xa[nt].x, xa[nt].y, xa16[nt].x, xa16[nt].y);
+          bad |= bf16x4_to_f16_pairs(xa[nt].z, xa[nt].w, xa16[nt].z, xa16[nt].w);
+          bad |= bf16x4_to_f16_pairs(xb[nt].x, xb[nt].y, xb16[nt].x, xb16[nt].y);
+          bad |= bf16x4_to_f16_pairs(xb[nt].z, xb[nt].w, xb16[nt].z, xb16[nt].w);
+        }
+        f16 = !__any_sync(0xffffffffu, bad != 0);
+      }
+      if (f16) {
+        mma_chunk<NT, true>(acc[0], ra0, rb0, xa16, xb16);
+        mma_chunk<NT, true>(acc[1], ra1, rb1, xa16, xb16);
+      } else {
+        mma_chunk<NT, false>(acc[0], ra0, rb0, xa, xb);
+        mma_chunk<NT, false>(acc[1], ra1, rb1, xa, xb);
+      }
     }
 
     // ------------------------------------------------------------ tile epilogue
@@ -562,10 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
 #pragma unroll
-      for (int bb = 0; bb < B; ++bb)
+      for (int bb = 0; bb < 4 / NMP; ++bb)  // warps (u = bb * NMP + warp / 2, h) hold m-tile pair warp / 2
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int src = 2 * ((warp >> 1) * B + bb) + hh;
+          const int src = 2 * (bb * NMP + (warp >> 1)) + hh;
           const float* o = sRed + ((src * 2 + (warp & 1)) * 32 + lane) * 4 * NT;
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
@@ -702,7 +724,6 @@ int fail(int code, const std::string& msg) {
 struct DeviceInfo {
   int ok = 0;             // 1 = checked and sm_100, -1 = wrong arch
   int sm_count = 0;
-  unsigned smem_set = 0;  // bit per kernel instance with the dynamic shared memory attribute set
 };
 std::mutex g_mu;
 DeviceInfo g_dev[64];
@@ -771,39 +792,58 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
   return QF_OK;
 }
 
-// Tile height: the widest of 128 / 64 / 32 rows that still gives every SM a whole tile.
-int pick_bn(int N, int sms) {
-  if ((N + 127) / 128 >= sms) return 128;
-  if ((N + 63) / 64 >= sms) return 64;
-  return 32;
+// Tile shape (BN rows x KS k-bytes per stage).  Longer contiguous runs per weight row stream faster from HBM3e
+// (512-byte runs reach the plain read rate, 128-byte runs about 80 % of it), narrow tiles cost activation copies
+// (2M/BN of the weight bytes) and per-tile epilogues, and too few tiles move work into stream-K splits.  The rule
+// below is the measured best (or within 3 %) on B200 over the Qwen decoder shapes and their 2/4/8-way shards at
+// M = 1, 5 and 16:
+//   N >= ~1.8 x 128 x SMs  (gate_up, vocab head)          -> 128 x 256
+//   N >= ~0.9 x 64 x SMs   (qkv, gate_up shards)          -> 64 x 512
+//   smaller N with N*K >= 5120*8704 (down, its 2-way shard) -> 64 x 512
+//   otherwise (o_proj, narrow shards)                      -> 32 x 1024
+void pick_tiles(int N, int K, int sms, int* bn, int* ks) {
+  const long long t128 = (N + 127) / 128, t64 = (N + 63) / 64;
+  if (10 * t128 >= 18LL * sms) {
+    *bn = 128;
+    *ks = 256;
+  } else if (10 * t64 >= 9LL * sms || static_cast<long long>(N) * K >= 5120LL * 8704) {
+    *bn = 64;
+    *ks = 512;
+  } else {
+    *bn = 32;
+    *ks = 1024;
+  }
 }
 
-template <int BN, int NT, bool HEAD>
-int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, unsigned flags,
-           cudaStream_t stream) {
-  using C = Geo<BN, NT>;
-  auto kern = w8a16_kernel<BN, NT, HEAD>;
-  const unsigned bit = 1u << ((BN == 128 ? 0 : BN == 64 ? 1 : 2) * 4 + (NT - 1) * 2 + (HEAD ? 1 : 0));
+template <int BN, int NT, int KS, bool HEAD>
+int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
+           unsigned flags, cudaStream_t stream) {
+  using C = Geo<BN, NT, KS>;
+  auto kern = w8a16_kernel<BN, NT, KS, HEAD>;
+  static bool smem_attr_set[64] = {};
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!(dinfo->smem_set & bit)) {
+    if (!smem_attr_set[dev]) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
       if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-      dinfo->smem_set |= bit;
+      smem_attr_set[dev] = true;
     }
   }
   CUtensorMap tw, tx;
   int rc = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
                      static_cast<uint64_t>(ldw), 128, BN);
   if (rc) return rc;
+  // activation boxes are M rows high: only the real tokens are copied
   const uint64_t xstride = (p.M > 1) ? static_cast<uint64_t>(ldx) * 2 : (static_cast<uint64_t>(p.K) * 2 + 15) / 16 * 16;
   rc = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M),
-                 xstride, 64, 8 * NT);
+                 xstride, 64, static_cast<uint32_t>(p.M));
   if (rc) return rc;
 
   p.f16_path = f16_path();
-  p.kiters = (p.K + C::KS - 1) / C::KS;
+  p.x_tx = static_cast<uint32_t>(2 * C::B * p.M * 128);
+  p.kiters = (p.K + KS - 1) / KS;
   p.ntiles = (p.N + BN - 1) / BN;
+  if (p.ntiles > kMaxTiles) return fail(QF_ERR_SHAPE, "too many tiles for this tile height");
   const long long total = static_cast<long long>(p.kiters) * p.ntiles;
   int G = dinfo->sm_count;
   if (G > kMaxGrid) G = kMaxGrid;
@@ -835,18 +875,41 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   return QF_OK;
 }
 
+template <int BN, int KS, bool HEAD>
+int launch_nt(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
+              unsigned flags, cudaStream_t st) {
+  if (p.M <= 8) return launch<BN, 1, KS, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  return launch<BN, 2, KS, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+}
+
+// Optional fixed tile shape (environment QF_TILES="BN:KS", read once; 0 = the per-shape choice): used by the
+// tests to run every kernel instance, and for tuning.
+struct TileShape {
+  int bn = 0, ks = 0;
+};
+const TileShape& tile_override() {
+  static const TileShape v = [] {
+    TileShape t;
+    if (const char* e = std::getenv("QF_TILES")) {
+      if (std::sscanf(e, "%d:%d", &t.bn, &t.ks) != 2) t = TileShape{};
+    }
+    return t;
+  }();
+  return v;
+}
+
 template <bool HEAD>
-int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo,
+int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
                unsigned flags, cudaStream_t st) {
-  const int bn = pick_bn(p.N, dinfo->sm_count);
-  if (p.M <= 8) {
-    if (bn == 128) return launch<128, 1, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
-    if (bn == 64) return launch<64, 1, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
-    return launch<32, 1, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
-  }
-  if (bn == 128) return launch<128, 2, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
-  if (bn == 64) return launch<64, 2, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
-  return launch<32, 2, HEAD>(x, ldx, w, ldw, p, dinfo, flags, st);
+  int bn = tile_override().bn, ks = tile_override().ks;
+  if (bn == 0) pick_tiles(p.N, p.K, dinfo->sm_count, &bn, &ks);
+  if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 512) return launch_nt<64, 512, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 512) return launch_nt<32, 512, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 1024) return launch_nt<32, 1024, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  return fail(QF_ERR_SHAPE, "no kernel instance for the chosen tile shape");
 }
 
 int check_common(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, int M, int N, int K,
@@ -914,7 +977,7 @@ int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
-  return launch_any<false>(x, ldx, w, ldw, p, dinfo, flags, st);
+  return launch_any<false>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
 int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* logits,
@@ -944,7 +1007,7 @@ int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
   p.row_max = row_max;
   p.row_argmax = reinterpret_cast<long long*>(row_argmax);
   p.row_lse = row_lse;
-  return launch_any<true>(x, ldx, w, ldw, p, dinfo, flags, static_cast<cudaStream_t>(stream));
+  return launch_any<true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
 }
 
 int qf_workspace_status(void* ws, void* stream, int* status) {
@@ -1069,5 +1132,5 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
     e = cudaGetLastError();
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
-  return launch_any<false>(x, ldx, w, ldw, p, dinfo, flags, st);
+  return launch_any<false>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }

@@ -1,6 +1,6 @@
-"""Run as ``python -m tests._grid_cap_case`` with QF_GRID_CAP set: GEMM and head shapes whose tiles are split
-between CTAs in ways the full grid never produces (one CTA, a few CTAs, stream-K shares of many stages),
-checked against the oracle.  Exits non-zero on a mismatch.  Used by test_gpu_schedule.py."""
+"""Run as ``python -m tests._grid_cap_case`` with QF_GRID_CAP or QF_TILES set: GEMM and head shapes whose
+tiles are split between CTAs in ways the full grid never produces (one CTA, a few CTAs, stream-K shares of many
+stages), or run on a forced tile shape, checked against the oracle.  Exits non-zero on a mismatch.  Used by test_gpu_schedule.py."""
 from __future__ import annotations
 
 import sys
