@@ -53,7 +53,7 @@ namespace qf {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kProducerWarp = 8;            // TMA issue (one lane)
-constexpr int kFixupWarp = 9;               // reduction of stream-K partial tiles
+constexpr int kEpilogueWarp = 9;            // tile epilogues and stream-K reductions
 constexpr int kThreads = 10 * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kMaxBN = 128;
@@ -61,10 +61,11 @@ constexpr int kMaxGrid = 256;
 constexpr int kMaxTiles = QF_MAX_N / kMaxBN;  // tile counters (tiles narrower than 128 rows only when N < 64*SMs)
 constexpr int kMaxSplit = 8;                // stream-K: at most about this many CTAs share a split tile
 constexpr int kBarConsumers = 1;            // named barriers (0 is __syncthreads)
-constexpr int kBarFix0 = 2;                 // consumers -> fixup warp, first partial SK tile
-constexpr int kBarFix1 = 3;                 // second partial SK tile
-constexpr int kBarEnd = 4;                  // consumers + fixup warp at the end (head only)
+constexpr int kBarReady = 2;                // consumers -> epilogue warp: a tile's partial sums are in sRed
+constexpr int kBarFree = 3;                 // epilogue warp -> consumers: sRed has been read
+constexpr int kBarEnd = 4;                  // consumers + epilogue warp at the end (head only)
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;  // 4 s
+constexpr uint64_t kPeerWaitNs = 100000ull;        // stream-K reducer: wait for the other CTAs' partials (100 us)
 
 // workspace layout (bytes); the prefix [0, kWsZeroBytes) must be zero before the first call
 constexpr size_t kWsHeader = 256;                              // [0] error flag, [2] CTAs done (head)
@@ -86,14 +87,17 @@ template <int BN, int NT, int KS> struct Geo {
   static constexpr int kStageBytes = kWBytes + kXStageBytes;
   static constexpr int kRedBytes = kConsumerWarps * 2 * 32 * 4 * NT * 4;  // [warp][m-tile of pair][lane][4NT]
   static constexpr int kStatBytes = 8 * 16 * 16;                          // float4 [m-tile][token]
-  static constexpr int kFixedBytes = kRedBytes + kStatBytes + 2 * 16 * 8 + 64 + 1024;
+  static constexpr int kOutStride = BN + 8;                               // bf16 [16 tokens][BN + 8] (padded)
+  static constexpr int kOutBytes = 16 * kOutStride * 2;
+  static constexpr int kFixedBytes = kRedBytes + kStatBytes + kOutBytes + 2 * 16 * 8 + 64 + 1024;
   static constexpr int kBudget = 226 * 1024;
   static constexpr int kStagesFit = (kBudget - kFixedBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 10 ? 10 : kStagesFit;
   static constexpr int kOffX = kStages * kWBytes;
   static constexpr int kOffRed = kOffX + kStages * kXStageBytes;
   static constexpr int kOffStat = kOffRed + kRedBytes;
-  static constexpr int kOffBar = kOffStat + kStatBytes;       // full[S], empty[S]
+  static constexpr int kOffOut = kOffStat + kStatBytes;
+  static constexpr int kOffBar = kOffOut + kOutBytes;         // full[S], empty[S]
   static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;  // abort, last
   static constexpr int kSmemBytes = kOffFlag + 64 + 1024;     // + alignment slack
   static_assert(BPW >= 1 && B * NMP == 4 * BPW, "the four warp pairs cover the stage's boxes evenly");
@@ -116,6 +120,7 @@ struct Params {
   uint8_t* ws;
   int f16_path;
   uint32_t x_tx;  // activation bytes per stage: 2 B boxes of M rows x 128 bytes
+  int out_vec;     // bf16 output rows (y or logits) can be written with 16-byte stores
   // head
   __nv_bfloat16* logits;
   int64_t ldl;
@@ -266,6 +271,184 @@ __device__ __forceinline__ RowStat warp_tile_stat(const Params& p, int n0, int n
   return st;
 }
 
+// Reduction of a stream-K tile from every contributor's slot (CTAs c_first .. c_last, in that order), by the
+// contributor that arrived last when the tile's designated reducer did not wait for the others: finishes the tile
+// (scale + store, or logits + tile statistics for the head) and re-arms the tile's counter.
+template <int BN, int NT, bool HEAD>
+__device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int lane, int c_first, int c_last,
+                                                 int* counters, const float* partials, float4* tile_stats) {
+  // Slot = [BN rows][8*NT tokens] fp32, read as float4: lane takes float4 f = lane + 32 j (row f / (2 NT),
+  // tokens 4 (lane % (2 NT)) + 0..3).  All of a contributor's loads (and those of U contributors) are issued
+  // before they are added, in ascending CTA order.
+  constexpr int F4 = BN * 2 * NT;
+  constexpr int PER = F4 / 32;
+  constexpr int PC = PER > 8 ? 8 : PER;   // float4 per lane per pass (bounded registers)
+  constexpr int U = PC >= 8 ? 1 : 8 / PC;  // contributors whose loads are in flight together
+  const int m_base = 4 * (lane % (2 * NT));
+  RowStat st[4];
+#pragma unroll
+  for (int pass = 0; pass < PER / PC; ++pass) {
+    float4 v[PC];
+#pragma unroll
+    for (int j = 0; j < PC; ++j) v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int cc = c_first; cc <= c_last; cc += U) {
+      float4 a[U][PC];
+#pragma unroll
+      for (int uu = 0; uu < U; ++uu) {
+        if (cc + uu <= c_last) {
+          const int ft = static_cast<int>(split_start(cc + uu, p.Tsk, p.Gsk) / p.kiters);
+          const float4* sl = reinterpret_cast<const float4*>(
+              partials + static_cast<size_t>(2 * (cc + uu) + (tile == ft ? 0 : 1)) * kPartialSlotFloats);
+#pragma unroll
+          for (int j = 0; j < PC; ++j) a[uu][j] = __ldcg(sl + lane + 32 * (pass * PC + j));
+        }
+      }
+#pragma unroll
+      for (int uu = 0; uu < U; ++uu) {
+        if (cc + uu <= c_last) {
+#pragma unroll
+          for (int j = 0; j < PC; ++j) {
+            v[j].x += a[uu][j].x;
+            v[j].y += a[uu][j].y;
+            v[j].z += a[uu][j].z;
+            v[j].w += a[uu][j].w;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < PC; ++j) {
+      const int n = tile * BN + (lane + 32 * (pass * PC + j)) / (2 * NT);
+      const float sc = n < p.N ? __ldg(p.scale + n) : 0.f;
+      const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int m = m_base + e;
+        if constexpr (!HEAD) {
+          store_out(p, n, m, vv[e] * sc);
+        } else {
+          const __nv_bfloat16 rv = __float2bfloat16_rn(vv[e] * sc);
+          if (p.logits && m < p.M && n < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n] = rv;
+          const RowStat one =
+              n < p.n_valid ? RowStat{__bfloat162float(rv), n, 1.f} : RowStat{-INFINITY, INT_MAX, 0.f};
+          st[e] = (pass == 0 && j == 0) ? one : stat_combine(st[e], one);
+        }
+      }
+    }
+  }
+  if constexpr (HEAD) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      RowStat sr = st[e];
+#pragma unroll
+      for (int off = 2 * NT; off < 32; off <<= 1) sr = stat_combine(sr, stat_shfl_xor(sr, off));
+      if (lane < 2 * NT)
+        tile_stats[static_cast<size_t>(tile) * 16 + m_base + e] = make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
+    }
+    __threadfence();
+  }
+  if (lane == 0) counters[tile] = 0;  // ready for the next call on this workspace
+}
+
+// Finishes a whole tile from the epilogue warp's fragment sums (lane (g, t): rows 16 mt + g and 16 mt + g + 8,
+// tokens 8 nt + 2 t and 8 nt + 2 t + 1): scale, bf16 rounding (+ the bias as a second rounding), rows staged in
+// shared memory and written with 16-byte stores (GEMM output or head logits), and for the head the tile's per-token
+// (max, first argmax, sum exp) of its bf16 logits.
+template <int BN, int NT, bool HEAD>
+__device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane, const float (&v)[BN / 16][NT][4],
+                                            const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* tile_stats) {
+  constexpr int MT = BN / 16;
+  constexpr int OS = BN + 8;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  if constexpr (!HEAD) {
+    if (p.y_f32) {  // fp32 export: plain stores
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int n0 = tile * BN + 16 * mt + g;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int m0 = 8 * nt + 2 * t;
+          store_out(p, n0, m0, v[mt][nt][0] * sc[mt][0]);
+          store_out(p, n0, m0 + 1, v[mt][nt][1] * sc[mt][0]);
+          store_out(p, n0 + 8, m0, v[mt][nt][2] * sc[mt][1]);
+          store_out(p, n0 + 8, m0 + 1, v[mt][nt][3] * sc[mt][1]);
+        }
+      }
+      return;
+    }
+  }
+  RowStat st[NT][2];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    const int n0 = tile * BN + 16 * mt + g;
+    const int n1 = n0 + 8;
+    float b0 = 0.f, b1 = 0.f;
+    if constexpr (!HEAD) {
+      if (p.bias) {
+        if (n0 < p.N) b0 = __bfloat162float(p.bias[n0]);
+        if (n1 < p.N) b1 = __bfloat162float(p.bias[n1]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int bq = 0; bq < 2; ++bq) {
+        const int m = 8 * nt + 2 * t + bq;
+        __nv_bfloat16 r0 = __float2bfloat16_rn(v[mt][nt][bq] * sc[mt][0]);
+        __nv_bfloat16 r1 = __float2bfloat16_rn(v[mt][nt][2 + bq] * sc[mt][1]);
+        if constexpr (!HEAD) {
+          if (p.bias) {
+            r0 = __float2bfloat16_rn(__bfloat162float(r0) + b0);
+            r1 = __float2bfloat16_rn(__bfloat162float(r1) + b1);
+          }
+        } else {
+          RowStat one{-INFINITY, INT_MAX, 0.f};
+          if (n0 < p.n_valid) one = RowStat{__bfloat162float(r0), n0, 1.f};
+          if (n1 < p.n_valid) one = stat_combine(one, RowStat{__bfloat162float(r1), n1, 1.f});
+          st[nt][bq] = (mt == 0) ? one : stat_combine(st[nt][bq], one);
+        }
+        sOut[m * OS + 16 * mt + g] = r0;
+        sOut[m * OS + 16 * mt + g + 8] = r1;
+      }
+  }
+  __syncwarp();
+  __nv_bfloat16* dst = HEAD ? p.logits : static_cast<__nv_bfloat16*>(p.y);
+  const int64_t ld = HEAD ? p.ldl : p.ldy;
+  if (dst) {
+    constexpr int CH = BN / 8;
+    for (int idx = lane; idx < p.M * CH; idx += 32) {
+      const int m = idx / CH;
+      const int ch = idx - m * CH;
+      const int n = tile * BN + ch * 8;
+      const __nv_bfloat16* src = sOut + m * OS + ch * 8;
+      __nv_bfloat16* out = dst + static_cast<int64_t>(m) * ld + n;
+      if (p.out_vec && n + 8 <= p.N) {
+        *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+      } else {
+        for (int e = 0; e < 8; ++e)
+          if (n + e < p.N) out[e] = src[e];
+      }
+    }
+  }
+  __syncwarp();  // staging tile free for the next tile
+  if constexpr (HEAD) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int bq = 0; bq < 2; ++bq) {
+        RowStat sr = st[nt][bq];
+        sr = stat_combine(sr, stat_shfl_xor(sr, 4));
+        sr = stat_combine(sr, stat_shfl_xor(sr, 8));
+        sr = stat_combine(sr, stat_shfl_xor(sr, 16));
+        if (g == 0)
+          tile_stats[static_cast<size_t>(tile) * 16 + 8 * nt + 2 * t + bq] =
+              make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
+      }
+    __threadfence();
+  }
+}
+
 template <int BN, int NT, int KS, bool HEAD>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
@@ -281,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sX = smem + C::kOffX;
   float* sRed = reinterpret_cast<float*>(smem + C::kOffRed);
   float4* sStat = reinterpret_cast<float4*>(smem + C::kOffStat);
+  __nv_bfloat16* sOut = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffOut);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kOffBar);  // TMA bytes of the stage landed
   uint64_t* empty_bar = full_bar + S;                                   // all consumer warps read the stage
   volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffFlag);
@@ -317,12 +501,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   StageIter it;
   it.init(p, cta);
   const int n_iter = it.n_iter;
-  // partial (stream-K) tiles of this CTA: the first and the last tile of its SK range, unless whole
+  // first and last tile of this CTA's stream-K range (partial unless the range covers them whole)
   const int sk_t0 = it.n_sk > 0 ? it.sk_begin / p.kiters : -1;
   const int sk_t1 = it.n_sk > 0 ? (it.sk_end - 1) / p.kiters : -1;
-  const bool part0 = it.n_sk > 0 && !(sk_t0 * p.kiters >= it.sk_begin && (sk_t0 + 1) * p.kiters <= it.sk_end);
-  const bool part1 = it.n_sk > 0 && sk_t1 != sk_t0 &&
-                     !(sk_t1 * p.kiters >= it.sk_begin && (sk_t1 + 1) * p.kiters <= it.sk_end);
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ producer (one lane)
@@ -387,96 +568,145 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* counters = reinterpret_cast<int*>(p.ws + kWsCounters);
   float* partials = reinterpret_cast<float*>(p.ws + kWsPartials);
   float4* tile_stats = reinterpret_cast<float4*>(p.ws + kWsStats);
+  // tile ends of this CTA: every tile its stream-K range touches, then its q whole tiles
+  const int n_ends = (it.n_sk > 0 ? sk_t1 - sk_t0 + 1 : 0) + p.q;
 
-  if (warp == kFixupWarp) {
-    // ------------------------------------------------------------------ fixup warp: stream-K partial tiles
+  if (warp == kEpilogueWarp) {
+    // ------------------------------------------------------------------ epilogue warp
+    // Walks the consumers' stage sequence; at each tile end it takes the eight consumer warps' partial sums from
+    // shared memory, adds them in a fixed order and finishes the tile while the consumers stream the next one.
+    // Stream-K tiles: a CTA that holds a later part of a tile (its first tile) stores its partial sums and counts
+    // itself in; the CTA holding the tile's first k-stages (its last stream-K tile, always the last to finish
+    // it) is the tile's reducer: it waits for the others' count, prefetches their sums while its own stages still
+    // stream, and finishes the tile.  If that wait exceeds kPeerWaitNs (CTAs not co-resident), the reducer hands
+    // off like the others and the last one to count itself in reduces every slot.
     pdl_wait();
-    for (int which = 0; which < 2; ++which) {
-      if (!(which == 0 ? part0 : part1)) continue;
-      const int tile = which == 0 ? sk_t0 : sk_t1;
-      named_bar_sync(which == 0 ? kBarFix0 : kBarFix1, kConsumerThreads + 32);  // this CTA's partial is written
-      const int it0 = tile * p.kiters;
-      const int c_first = cta_of(it0, p.Tsk, p.Gsk);
-      const int c_last = cta_of(min(it0 + p.kiters, p.Tsk) - 1, p.Tsk, p.Gsk);
-      int last = 0;
-      if (lane == 0) {
-        __threadfence();
-        last = atomicAdd(&counters[tile], 1) == c_last - c_first;
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    int tc = -1, tr = -1;  // this CTA's contributor tile and reducer tile
+    if (it.n_sk > 0) {
+#pragma unroll
+      for (int side = 0; side < 2; ++side) {
+        const int tt = side == 0 ? sk_t0 : sk_t1;
+        if (side == 1 && tt == sk_t0) break;
+        const bool whole_tt = tt * p.kiters >= it.sk_begin && (tt + 1) * p.kiters <= it.sk_end;
+        if (whole_tt) continue;
+        if (tt * p.kiters >= it.sk_begin) tr = tt;
+        else tc = tt;
       }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) continue;
-      __threadfence();
-      // Slot = [BN rows][8*NT tokens] fp32, read as float4: lane takes float4 f = lane + 32 j (row f / (2 NT),
-      // tokens 4 (lane % (2 NT)) + 0..3).  All of a contributor's loads (and those of U contributors) are issued
-      // before they are added, in ascending CTA order.
-      constexpr int F4 = BN * 2 * NT;
-      constexpr int PER = F4 / 32;
-      constexpr int PC = PER > 8 ? 8 : PER;   // float4 per lane per pass (bounded registers)
-      constexpr int U = PC >= 8 ? 1 : 8 / PC;  // contributors whose loads are in flight together
-      const int m_base = 4 * (lane % (2 * NT));
-      RowStat st[4];
+    }
+    StageIter et = it;
+    int tcount = 0;
+    for (int i = 0; i < n_iter; ++i) {
+      const int tile = et.tile;
+      const bool sk = et.sk;
+      const bool tile_end = (et.kk == p.kiters - 1) || (sk && i == et.n_sk - 1);
+      et.next(p);
+      if (!tile_end) continue;
+      const bool is_red = sk && tile == tr;
+      const bool is_con = sk && tile == tc;
+      float sc[MT][2];
 #pragma unroll
-      for (int pass = 0; pass < PER / PC; ++pass) {
-        float4 v[PC];
+      for (int mt = 0; mt < MT; ++mt) {
+        const int n0 = tile * BN + 16 * mt + g;
+        sc[mt][0] = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
+        sc[mt][1] = n0 + 8 < p.N ? __ldg(p.scale + n0 + 8) : 0.f;
+      }
+      int c_first = 0, c_last = 0;
+      if (is_red || is_con) {
+        const int it0 = tile * p.kiters;
+        c_first = cta_of(it0, p.Tsk, p.Gsk);
+        c_last = cta_of(min(it0 + p.kiters, p.Tsk) - 1, p.Tsk, p.Gsk);
+      }
+      // the tile's sums: the reducer starts from the later CTAs' partials (in CTA order), then adds its own
+      float v[MT][NT][4];
 #pragma unroll
-        for (int j = 0; j < PC; ++j) v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int cc = c_first; cc <= c_last; cc += U) {
-          float4 a[U][PC];
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int uu = 0; uu < U; ++uu) {
-            if (cc + uu <= c_last) {
-              const int ft = static_cast<int>(split_start(cc + uu, p.Tsk, p.Gsk) / p.kiters);
-              const float4* sl = reinterpret_cast<const float4*>(
-                  partials + static_cast<size_t>(2 * (cc + uu) + (tile == ft ? 0 : 1)) * kPartialSlotFloats);
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-              for (int j = 0; j < PC; ++j) a[uu][j] = __ldcg(sl + lane + 32 * (pass * PC + j));
+          for (int e = 0; e < 4; ++e) v[mt][nt][e] = 0.f;
+      bool red_ok = false;
+      if (is_red) {
+        int ok = 0;
+        if (lane == 0) {
+          const int want = c_last - c_first;
+          const uint64_t t0 = global_timer_ns();
+          while (true) {
+            if (ld_acquire_gpu(counters + tile) == want) {
+              ok = 1;
+              break;
             }
+            if (global_timer_ns() - t0 > kPeerWaitNs) break;
+            sleep_ns(128);
           }
+        }
+        red_ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
+        if (red_ok) {
+#pragma unroll 2
+          for (int cc = c_first + 1; cc <= c_last; ++cc) {  // the tile is each later CTA's first: slot 0
+            const float* sl = partials + static_cast<size_t>(2 * cc) * kPartialSlotFloats;
 #pragma unroll
-          for (int uu = 0; uu < U; ++uu) {
-            if (cc + uu <= c_last) {
+            for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-              for (int j = 0; j < PC; ++j) {
-                v[j].x += a[uu][j].x;
-                v[j].y += a[uu][j].y;
-                v[j].z += a[uu][j].z;
-                v[j].w += a[uu][j].w;
+              for (int nt = 0; nt < NT; ++nt) {
+                const int row = 16 * mt + g;
+                const int col = 8 * nt + 2 * t;
+                const float2 a = __ldcg(reinterpret_cast<const float2*>(sl + row * 8 * NT + col));
+                const float2 b = __ldcg(reinterpret_cast<const float2*>(sl + (row + 8) * 8 * NT + col));
+                v[mt][nt][0] += a.x;
+                v[mt][nt][1] += a.y;
+                v[mt][nt][2] += b.x;
+                v[mt][nt][3] += b.y;
               }
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < PC; ++j) {
-          const int n = tile * BN + (lane + 32 * (pass * PC + j)) / (2 * NT);
-          const float sc = n < p.N ? __ldg(p.scale + n) : 0.f;
-          const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int m = m_base + e;
-            if constexpr (!HEAD) {
-              store_out(p, n, m, vv[e] * sc);
-            } else {
-              const __nv_bfloat16 rv = __float2bfloat16_rn(vv[e] * sc);
-              if (p.logits && m < p.M && n < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n] = rv;
-              const RowStat one =
-                  n < p.n_valid ? RowStat{__bfloat162float(rv), n, 1.f} : RowStat{-INFINITY, INT_MAX, 0.f};
-              st[e] = (pass == 0 && j == 0) ? one : stat_combine(st[e], one);
-            }
           }
         }
       }
-      if constexpr (HEAD) {
+      named_bar_sync(kBarReady, kConsumerThreads + 32);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          RowStat s = st[e];
+      for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
-          for (int off = 2 * NT; off < 32; off <<= 1) s = stat_combine(s, stat_shfl_xor(s, off));
-          if (lane < 2 * NT)
-            tile_stats[static_cast<size_t>(tile) * 16 + m_base + e] = make_float4(s.m, __int_as_float(s.a), s.s, 0.f);
-        }
+        for (int bb = 0; bb < 4 / NMP; ++bb)  // warps (u = bb * NMP + mt / 2, h) hold m-tile mt
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int src = 2 * (bb * NMP + (mt >> 1)) + hh;
+            const float* o = sRed + ((src * 2 + (mt & 1)) * 32 + lane) * 4 * NT;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) v[mt][nt][e] += o[nt * 4 + e];
+          }
+      }
+      if (tcount + 1 < n_ends) named_bar_arrive(kBarFree, kConsumerThreads + 32);
+      ++tcount;
+
+      if (is_red && red_ok) {
+        if (lane == 0) counters[tile] = 0;  // every other contributor has counted itself in: re-arm
+      } else if (is_red || is_con) {
+        const int which = (tile == sk_t0) ? 0 : 1;
+        float* slot = partials + static_cast<size_t>(2 * cta + which) * kPartialSlotFloats;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {  // [BN rows][8*NT tokens]
+            const int row = 16 * mt + g;
+            const int col = 8 * nt + 2 * t;
+            __stcg(reinterpret_cast<float2*>(slot + row * 8 * NT + col), make_float2(v[mt][nt][0], v[mt][nt][1]));
+            __stcg(reinterpret_cast<float2*>(slot + (row + 8) * 8 * NT + col),
+                   make_float2(v[mt][nt][2], v[mt][nt][3]));
+          }
         __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(counters + tile, 1) == c_last - c_first;  // only after a reducer gave up
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          split_reduce_all<BN, NT, HEAD>(p, tile, lane, c_first, c_last, counters, partials, tile_stats);
+        }
+        continue;
       }
-      if (lane == 0) counters[tile] = 0;  // ready for the next call on this workspace
+      finish_tile<BN, NT, HEAD>(p, tile, lane, v, sc, sOut, tile_stats);
     }
     if constexpr (HEAD) named_bar_sync(kBarEnd, kConsumerThreads + 32);
     return;
@@ -500,6 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
   const int ctid = threadIdx.x;  // 0..255 among consumers
   const bool use_f16 = p.f16_path != 0;
+  int tcount = 0;
 
   float acc[2][NT][4];
 #pragma unroll
@@ -555,14 +786,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
-    // ------------------------------------------------------------ tile epilogue
-    const int tile = it.tile;
-    const bool sk = it.sk;
-    const bool tile_end = (it.kk == p.kiters - 1) || (sk && i == it.n_sk - 1);
+    // ------------------------------------------------------------ tile end: hand the sums to the epilogue warp
+    const bool tile_end = (it.kk == p.kiters - 1) || (it.sk && i == it.n_sk - 1);
     it.next(p);
     if (!tile_end) continue;
-
-    // every warp dumps its two m-tile partials; warp w < MT then owns m-tile w
+    if (tcount > 0) named_bar_sync(kBarFree, kConsumerThreads + 32);  // the previous tile's sums have been read
     {
       float* mine = sRed + (warp * 2 * 32 + lane) * 4 * NT;
 #pragma unroll
@@ -575,94 +803,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[j][nt][e] = 0.f;
           }
     }
-    named_bar_sync(kBarConsumers, kConsumerThreads);
-    float v[NT][4];
-    const bool owner = warp < MT;
-    if (owner) {
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
-#pragma unroll
-      for (int bb = 0; bb < 4 / NMP; ++bb)  // warps (u = bb * NMP + warp / 2, h) hold m-tile pair warp / 2
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int src = 2 * (bb * NMP + (warp >> 1)) + hh;
-          const float* o = sRed + ((src * 2 + (warp & 1)) * 32 + lane) * 4 * NT;
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[nt][e] += o[nt * 4 + e];
-        }
-    }
-    const int rl0 = 16 * warp + g;  // owner's rows rl0 and rl0 + 8 of the tile
-    const int tile_it0 = tile * p.kiters;
-    const bool whole = !sk || (tile_it0 >= it.sk_begin && tile_it0 + p.kiters <= it.sk_end);
-    if (!whole) {
-      // stream-K partial: store it and hand the reduction to the fixup warp
-      if (owner) {
-        const int which = (tile == sk_t0) ? 0 : 1;
-        float* slot = partials + static_cast<size_t>(2 * cta + which) * kPartialSlotFloats;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {  // [BN rows][8*NT tokens]
-          const int col = 8 * nt + 2 * t;
-          *reinterpret_cast<float2*>(slot + rl0 * 8 * NT + col) = make_float2(v[nt][0], v[nt][1]);
-          *reinterpret_cast<float2*>(slot + (rl0 + 8) * 8 * NT + col) = make_float2(v[nt][2], v[nt][3]);
-        }
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);  // sRed reads done before the next tile's dump
-      named_bar_arrive(tile == sk_t0 ? kBarFix0 : kBarFix1, kConsumerThreads + 32);
-      continue;
-    }
-
-    const int n0 = tile * BN + rl0;
-    const int n1 = n0 + 8;
-    if constexpr (!HEAD) {
-      if (owner) {
-        const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
-        const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int m0 = 8 * nt + 2 * t;
-          store_out(p, n0, m0, v[nt][0] * s0);
-          store_out(p, n0, m0 + 1, v[nt][1] * s0);
-          store_out(p, n1, m0, v[nt][2] * s1);
-          store_out(p, n1, m0 + 1, v[nt][3] * s1);
-        }
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);  // sRed reads done before the next tile's dump
-    } else {
-      if (owner) {
-        const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
-        const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-          for (int bq = 0; bq < 2; ++bq) {
-            const int m = 8 * nt + 2 * t + bq;
-            const __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][bq] * s0);
-            const __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + bq] * s1);
-            if (p.logits && m < p.M) {
-              if (n0 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n0] = r0;
-              if (n1 < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n1] = r1;
-            }
-            const RowStat st = warp_tile_stat(p, n0, n1, r0, r1);
-            if (g == 0) sStat[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
-          }
-        }
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (warp == 0 && lane < 8 * NT) {
-        RowStat st{-INFINITY, INT_MAX, 0.f};
-        for (int w = 0; w < MT; ++w) {
-          const float4 f = sStat[w * 16 + lane];
-          st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
-        }
-        tile_stats[static_cast<size_t>(tile) * 16 + lane] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
-        __threadfence();
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);  // sRed / sStat reuse by the next tile
-    }
+    named_bar_arrive(kBarReady, kConsumerThreads + 32);
+    ++tcount;
   }
 
   if constexpr (HEAD) {
@@ -676,15 +818,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (*sLast) {
       __threadfence();
-      for (int m = 0; m < p.M; ++m) {
-        RowStat st{-INFINITY, INT_MAX, 0.f};
-        for (int j = ctid; j < p.ntiles; j += kConsumerThreads) {
-          const float4 f = __ldcg(tile_stats + static_cast<size_t>(j) * 16 + m);
-          st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
-        }
+      // thread ctid folds tiles ctid, ctid + 256, ... for every row (all rows' loads of a tile in flight at once)
+      RowStat st[16];
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) st = stat_combine(st, stat_shfl_xor(st, off));
-        if (lane == 0) sStat[warp * 16 + m] = make_float4(st.m, __int_as_float(st.a), st.s, 0.f);
+      for (int m = 0; m < 16; ++m) st[m] = RowStat{-INFINITY, INT_MAX, 0.f};
+      for (int j = ctid; j < p.ntiles; j += kConsumerThreads) {
+        float4 f[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m < p.M) f[m] = __ldcg(tile_stats + static_cast<size_t>(j) * 16 + m);
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m < p.M) st[m] = stat_combine(st[m], RowStat{f[m].x, __float_as_int(f[m].y), f[m].z});
+      }
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        if (m < p.M) {
+          RowStat sr = st[m];
+#pragma unroll
+          for (int off = 1; off < 32; off <<= 1) sr = stat_combine(sr, stat_shfl_xor(sr, off));
+          if (lane == 0) sStat[warp * 16 + m] = make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
+        }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
       if (warp == 0 && lane < p.M) {
@@ -966,6 +1120,7 @@ int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
   p.y = y;
   p.ldy = ldy;
   p.y_f32 = y_dtype == QF_DTYPE_F32;
+  p.out_vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (M == 1 || ldy % 8 == 0);
   p.M = M;
   p.N = N;
   p.K = K;
@@ -1002,6 +1157,7 @@ int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
   p.ws = static_cast<uint8_t*>(ws);
   p.logits = static_cast<__nv_bfloat16*>(logits);
   p.ldl = ldl;
+  p.out_vec = reinterpret_cast<uintptr_t>(logits) % 16 == 0 && (M == 1 || ldl % 8 == 0);
   p.n_valid = n_valid;
   p.vocab_offset = vocab_offset;
   p.row_max = row_max;
@@ -1122,6 +1278,7 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
   p.y = y;
   p.ldy = ldy;
   p.y_f32 = y_dtype == QF_DTYPE_F32;
+  p.out_vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (M == 1 || ldy % 8 == 0);
   p.M = M;
   p.N = N;
   p.K = K;
