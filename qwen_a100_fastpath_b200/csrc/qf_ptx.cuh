@@ -85,6 +85,14 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
   return v;
 }
 __device__ __forceinline__ void sleep_ns(uint32_t ns) { asm volatile("nanosleep.u32 %0;" ::"r"(ns)); }
+// Atomic add with acquire + release semantics at GPU scope: the caller's earlier writes (and those ordered before
+// it by a CTA or warp barrier) are visible to whoever observes the new value, and writes released by earlier
+// adders are visible to the caller afterwards.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* ptr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
+}
 
 // ---- named barriers (id 0 is __syncthreads) -----------------------------------------------------
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

@@ -73,7 +73,8 @@ constexpr size_t kWsCounters = kWsHeader;                       // int32[kMaxTil
 constexpr size_t kWsZeroBytes = kWsCounters + sizeof(int) * kMaxTiles;
 constexpr size_t kWsPartials = (kWsZeroBytes + 1023) / 1024 * 1024;
 constexpr size_t kPartialSlotFloats = kMaxBN * 16;              // [BN rows][8*NT tokens]
-constexpr size_t kWsStats = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kMaxGrid;
+constexpr size_t kWsCtaStats = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kMaxGrid;  // head
+constexpr size_t kWsBytes = kWsCtaStats + sizeof(float4) * 16 * kMaxGrid;  // float4 [16 tokens][kMaxGrid CTAs]
 
 template <int BN, int NT, int KS> struct Geo {
   static constexpr int B = KS / 128;                            // 128-byte weight boxes per stage
@@ -259,16 +260,16 @@ __device__ __forceinline__ void mma_chunk(float (&acc)[NT][4], const uint4& ra, 
   }
 }
 
-// Statistics of one bf16 logit row pair (rows n0, n0 + 8 of a token column) reduced over the 8 lanes g.
-__device__ __forceinline__ RowStat warp_tile_stat(const Params& p, int n0, int n1, __nv_bfloat16 r0,
-                                                  __nv_bfloat16 r1) {
-  RowStat st{-INFINITY, INT_MAX, 0.f};
-  if (n0 < p.n_valid) st = RowStat{__bfloat162float(r0), n0, 1.f};
-  if (n1 < p.n_valid) st = stat_combine(st, RowStat{__bfloat162float(r1), n1, 1.f});
-  st = stat_combine(st, stat_shfl_xor(st, 4));
-  st = stat_combine(st, stat_shfl_xor(st, 8));
-  st = stat_combine(st, stat_shfl_xor(st, 16));
-  return st;
+// (max, first argmax) of bf16 logits: larger value wins, equal values keep the smaller column.
+struct MaxArg {
+  float m;
+  int a;
+};
+__device__ __forceinline__ MaxArg ma_max(const MaxArg& x, const MaxArg& y) {
+  return (y.m > x.m || (y.m == x.m && y.a < x.a)) ? y : x;
+}
+__device__ __forceinline__ MaxArg ma_shfl_xor(const MaxArg& v, int mask) {
+  return MaxArg{__shfl_xor_sync(0xffffffffu, v.m, mask), __shfl_xor_sync(0xffffffffu, v.a, mask)};
 }
 
 // Reduction of a stream-K tile from every contributor's slot (CTAs c_first .. c_last, in that order), by the
@@ -276,7 +277,7 @@ __device__ __forceinline__ RowStat warp_tile_stat(const Params& p, int n0, int n
 // (scale + store, or logits + tile statistics for the head) and re-arms the tile's counter.
 template <int BN, int NT, bool HEAD>
 __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int lane, int c_first, int c_last,
-                                                 int* counters, const float* partials, float4* tile_stats) {
+                                                 int* counters, const float* partials, float4* sTile) {
   // Slot = [BN rows][8*NT tokens] fp32, read as float4: lane takes float4 f = lane + 32 j (row f / (2 NT),
   // tokens 4 (lane % (2 NT)) + 0..3).  All of a contributor's loads (and those of U contributors) are issued
   // before they are added, in ascending CTA order.
@@ -343,9 +344,8 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
 #pragma unroll
       for (int off = 2 * NT; off < 32; off <<= 1) sr = stat_combine(sr, stat_shfl_xor(sr, off));
       if (lane < 2 * NT)
-        tile_stats[static_cast<size_t>(tile) * 16 + m_base + e] = make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
+        sTile[m_base + e] = make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
     }
-    __threadfence();
   }
   if (lane == 0) counters[tile] = 0;  // ready for the next call on this workspace
 }
@@ -356,7 +356,7 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
 // (max, first argmax, sum exp) of its bf16 logits.
 template <int BN, int NT, bool HEAD>
 __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane, const float (&v)[BN / 16][NT][4],
-                                            const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* tile_stats) {
+                                            const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* sTile) {
   constexpr int MT = BN / 16;
   constexpr int OS = BN + 8;
   const int g = lane >> 2;
@@ -378,7 +378,11 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
       return;
     }
   }
-  RowStat st[NT][2];
+  MaxArg mx[NT][2];  // head: per token 8 nt + 2 t + bq over this lane's rows
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int bq = 0; bq < 2; ++bq) mx[nt][bq] = MaxArg{-INFINITY, INT_MAX};
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
     const int n0 = tile * BN + 16 * mt + g;
@@ -403,10 +407,8 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
             r1 = __float2bfloat16_rn(__bfloat162float(r1) + b1);
           }
         } else {
-          RowStat one{-INFINITY, INT_MAX, 0.f};
-          if (n0 < p.n_valid) one = RowStat{__bfloat162float(r0), n0, 1.f};
-          if (n1 < p.n_valid) one = stat_combine(one, RowStat{__bfloat162float(r1), n1, 1.f});
-          st[nt][bq] = (mt == 0) ? one : stat_combine(st[nt][bq], one);
+          if (n0 < p.n_valid) mx[nt][bq] = ma_max(mx[nt][bq], MaxArg{__bfloat162float(r0), n0});
+          if (n1 < p.n_valid) mx[nt][bq] = ma_max(mx[nt][bq], MaxArg{__bfloat162float(r1), n1});
         }
         sOut[m * OS + 16 * mt + g] = r0;
         sOut[m * OS + 16 * mt + g + 8] = r1;
@@ -433,20 +435,61 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
   }
   __syncwarp();  // staging tile free for the next tile
   if constexpr (HEAD) {
+    // pass 1: the tile's max / first argmax per token over the 8 lanes g; pass 2: sum of exp(v - max) (one
+    // exponential per logit), added over g in a fixed order
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int bq = 0; bq < 2; ++bq) {
-        RowStat sr = st[nt][bq];
-        sr = stat_combine(sr, stat_shfl_xor(sr, 4));
-        sr = stat_combine(sr, stat_shfl_xor(sr, 8));
-        sr = stat_combine(sr, stat_shfl_xor(sr, 16));
-        if (g == 0)
-          tile_stats[static_cast<size_t>(tile) * 16 + 8 * nt + 2 * t + bq] =
-              make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
+        mx[nt][bq] = ma_max(mx[nt][bq], ma_shfl_xor(mx[nt][bq], 4));
+        mx[nt][bq] = ma_max(mx[nt][bq], ma_shfl_xor(mx[nt][bq], 8));
+        mx[nt][bq] = ma_max(mx[nt][bq], ma_shfl_xor(mx[nt][bq], 16));
       }
-    __threadfence();
+    float se[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int bq = 0; bq < 2; ++bq) se[nt][bq] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const int n0 = tile * BN + 16 * mt + g;
+      const int n1 = n0 + 8;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int bq = 0; bq < 2; ++bq) {
+          const float mref = mx[nt][bq].m;
+          if (mref != -INFINITY) {
+            const float r0 = __bfloat162float(__float2bfloat16_rn(v[mt][nt][bq] * sc[mt][0]));
+            const float r1 = __bfloat162float(__float2bfloat16_rn(v[mt][nt][2 + bq] * sc[mt][1]));
+            if (n0 < p.n_valid) se[nt][bq] += expf(r0 - mref);
+            if (n1 < p.n_valid) se[nt][bq] += expf(r1 - mref);
+          }
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int bq = 0; bq < 2; ++bq) {
+        float sum = se[nt][bq];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        if (g == 0)
+          sTile[8 * nt + 2 * t + bq] = make_float4(mx[nt][bq].m, __int_as_float(mx[nt][bq].a), sum, 0.f);
+      }
   }
+}
+
+// Head: folds a finished tile's per-token statistics (sTile[m], written by the epilogue warp) into lane m's running
+// statistics of this CTA, in the order the CTA finishes its tiles.
+__device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTile, RowStat& run) {
+  __syncwarp();
+  if (lane < p.M) {
+    const float4 f = sTile[lane];
+    run = stat_combine(run, RowStat{f.x, __float_as_int(f.y), f.z});
+  }
+  __syncwarp();
 }
 
 template <int BN, int NT, int KS, bool HEAD>
@@ -567,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int* counters = reinterpret_cast<int*>(p.ws + kWsCounters);
   float* partials = reinterpret_cast<float*>(p.ws + kWsPartials);
-  float4* tile_stats = reinterpret_cast<float4*>(p.ws + kWsStats);
+  float4* cta_stats = reinterpret_cast<float4*>(p.ws + kWsCtaStats);
   // tile ends of this CTA: every tile its stream-K range touches, then its q whole tiles
   const int n_ends = (it.n_sk > 0 ? sk_t1 - sk_t0 + 1 : 0) + p.q;
 
@@ -597,6 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     StageIter et = it;
     int tcount = 0;
+    RowStat run{-INFINITY, INT_MAX, 0.f};  // head: lane m folds token m's statistics over this CTA's tiles
     for (int i = 0; i < n_iter; ++i) {
       const int tile = et.tile;
       const bool sk = et.sk;
@@ -642,6 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         red_ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
+        __syncwarp();  // lane 0's acquire orders the other lanes' loads of the peers' slots
         if (red_ok) {
 #pragma unroll 2
           for (int cc = c_first + 1; cc <= c_last; ++cc) {  // the tile is each later CTA's first: slot 0
@@ -695,20 +740,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             __stcg(reinterpret_cast<float2*>(slot + (row + 8) * 8 * NT + col),
                    make_float2(v[mt][nt][2], v[mt][nt][3]));
           }
-        __threadfence();
-        __syncwarp();
+        __syncwarp();  // the slot stores of all lanes precede lane 0's release
         int last = 0;
-        if (lane == 0) last = atomicAdd(counters + tile, 1) == c_last - c_first;  // only after a reducer gave up
+        if (lane == 0)  // last only after a reducer gave up waiting
+          last = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t*>(counters + tile), 1u) ==
+                 static_cast<uint32_t>(c_last - c_first);
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          __threadfence();
-          split_reduce_all<BN, NT, HEAD>(p, tile, lane, c_first, c_last, counters, partials, tile_stats);
+          split_reduce_all<BN, NT, HEAD>(p, tile, lane, c_first, c_last, counters, partials, sStat);
+          if constexpr (HEAD) fold_tile(p, lane, sStat, run);
         }
         continue;
       }
-      finish_tile<BN, NT, HEAD>(p, tile, lane, v, sc, sOut, tile_stats);
+      finish_tile<BN, NT, HEAD>(p, tile, lane, v, sc, sOut, sStat);
+      if constexpr (HEAD) fold_tile(p, lane, sStat, run);
     }
-    if constexpr (HEAD) named_bar_sync(kBarEnd, kConsumerThreads + 32);
+    if constexpr (HEAD) {
+      if (lane < p.M) cta_stats[lane * kMaxGrid + cta] = make_float4(run.m, __int_as_float(run.a), run.s, 0.f);
+      named_bar_sync(kBarEnd, kConsumerThreads + 32);
+    }
     return;
   }
 
@@ -809,47 +859,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if constexpr (HEAD) {
     // the CTA that finishes last folds the per-tile statistics of all tiles (fixed order)
+    // kBarEnd orders every tile-statistics store of this CTA before thread 0's release; the last CTA's acquire
+    // (and the barrier after it) orders its reads after all CTAs' stores.
     named_bar_sync(kBarEnd, kConsumerThreads + 32);
     if (ctid == 0) {
-      __threadfence();
-      const unsigned old = atomicAdd(reinterpret_cast<unsigned*>(p.ws) + 2, 1u);
-      *sLast = (old == static_cast<unsigned>(p.G - 1)) ? 1 : 0;
+      const uint32_t old = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t*>(p.ws) + 2, 1u);
+      *sLast = (old == static_cast<uint32_t>(p.G - 1)) ? 1 : 0;
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (*sLast) {
-      __threadfence();
-      // thread ctid folds tiles ctid, ctid + 256, ... for every row (all rows' loads of a tile in flight at once)
-      RowStat st[16];
+      // Warp w folds tokens w and w + 8: lane l combines CTAs l, l + 32, ... in order, then a butterfly over the
+      // lanes.  The combine is symmetric, so every lane ends with the same bits, and the order is fixed.
 #pragma unroll
-      for (int m = 0; m < 16; ++m) st[m] = RowStat{-INFINITY, INT_MAX, 0.f};
-      for (int j = ctid; j < p.ntiles; j += kConsumerThreads) {
-        float4 f[16];
-#pragma unroll
-        for (int m = 0; m < 16; ++m)
-          if (m < p.M) f[m] = __ldcg(tile_stats + static_cast<size_t>(j) * 16 + m);
-#pragma unroll
-        for (int m = 0; m < 16; ++m)
-          if (m < p.M) st[m] = stat_combine(st[m], RowStat{f[m].x, __float_as_int(f[m].y), f[m].z});
-      }
-#pragma unroll
-      for (int m = 0; m < 16; ++m) {
+      for (int k = 0; k < 2; ++k) {
+        const int m = warp + kConsumerWarps * k;
         if (m < p.M) {
-          RowStat sr = st[m];
+          RowStat st{-INFINITY, INT_MAX, 0.f};
+          for (int c = lane; c < p.G; c += 32) {
+            const float4 f = __ldcg(cta_stats + m * kMaxGrid + c);
+            st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
+          }
 #pragma unroll
-          for (int off = 1; off < 32; off <<= 1) sr = stat_combine(sr, stat_shfl_xor(sr, off));
-          if (lane == 0) sStat[warp * 16 + m] = make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
+          for (int off = 16; off >= 1; off >>= 1) st = stat_combine(st, stat_shfl_xor(st, off));
+          if (lane == 0) {
+            p.row_max[m] = st.m;
+            p.row_argmax[m] = static_cast<long long>(st.a) + p.vocab_offset;
+            p.row_lse[m] = st.m + logf(st.s);
+          }
         }
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (warp == 0 && lane < p.M) {
-        RowStat st{-INFINITY, INT_MAX, 0.f};
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          const float4 f = sStat[w * 16 + lane];
-          st = stat_combine(st, RowStat{f.x, __float_as_int(f.y), f.z});
-        }
-        p.row_max[lane] = st.m;
-        p.row_argmax[lane] = static_cast<long long>(st.a) + p.vocab_offset;
-        p.row_lse[lane] = st.m + logf(st.s);
       }
       if (ctid == 0) reinterpret_cast<unsigned*>(p.ws)[2] = 0u;
     }
@@ -1096,9 +1133,8 @@ extern "C" {
 size_t qf_w8a16_workspace_bytes(int M, int N, int K) {
   (void)M;
   (void)K;
-  // head statistics: 16 float4 per tile, sized for the narrowest tiles (32 rows)
-  const size_t ntiles = N > 0 ? (static_cast<size_t>(N) + 31) / 32 : 0;
-  return kWsStats + ntiles * 16 * sizeof(float4);
+  (void)N;
+  return kWsBytes;
 }
 
 int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, const void* bias,

@@ -42,8 +42,8 @@ def test_abi_version_and_strerror():
 def test_workspace_bytes_layout():
     small = _lib.LIB.qf_w8a16_workspace_bytes(1, 128, 128)
     big = _lib.LIB.qf_w8a16_workspace_bytes(16, 151936, 5120)
-    assert 0 < small < big
-    assert big - small == (151936 // 32 - 128 // 32) * 256  # head statistics: 16 float4 per (32-row) tile
+    assert 0 < small == big  # fixed size: tile counters, stream-K partial slots, per-CTA head statistics
+    assert big < 8 << 20
 
 
 FAKE = 1 << 20  # a 16-byte-aligned non-null address; validation rejects before dereferencing anything
