@@ -215,14 +215,17 @@ class Step:
                 return alg_bytes(*shard(N, K, st, self.world), self.M)
         raise KeyError(name)
 
-    def run(self, linear=None, events=None):
+    def run(self, linear=None, events=None, phase_events=None):
         """Enqueue the step.  ``linear(x, w_t, s) -> y`` replaces the GEMM call (the public op allocates its
-        output); ``events`` records a CUDA event after every launch (instrumented pass)."""
+        output); ``events`` records a CUDA event after every launch (instrumented pass, PDL off);
+        ``phase_events`` records three events: step start, after the last decoder GEMM, after the head."""
         torch = self.torch
         from qwen_a100_fastpath_b200 import tp
         from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_mm
         if events is not None:
             events[0].record()
+        if phase_events is not None:
+            phase_events[0].record()
         e = 1
         for ws in self.layers:
             for name, _, _, style in LAYER:
@@ -236,11 +239,15 @@ class Step:
                     e += 1
                 if style == "row" and self.world > 1:
                     tp.all_reduce_partial(y)
+        if phase_events is not None:
+            phase_events[1].record()
         w, s = self.head_w
         w8a16_head(self.hidden, w, s, n_valid=self.head_n, vocab_offset=self.rank * self.head_n, pdl=self.pdl,
                    out=(self.logits, self.row_max, self.row_arg, self.row_lse))
         if events is not None:
             events[e].record()
+        if phase_events is not None:
+            phase_events[2].record()
         if self.world > 1:
             mx, am, lse = tp.gather_head_stats(self.row_max, self.row_arg, self.row_lse, out=self.gathered)
             self.row_max.copy_(mx)
@@ -333,7 +340,34 @@ def run_ours(args, rank: int, world: int, local: int):
     total_bytes = st.bytes_rank * world
     value = total_bytes / (ms * 1e-3) / 1e9
 
-    # ---- per-launch durations of the dominant kernel: instrumented replay (events between launches)
+    # ---- per-launch durations of the dominant kernel
+    # (1) the step as timed (PDL on), with events only at the step start, after the last decoder GEMM and after
+    #     the head: the decoder-GEMM phase / its launch count is the kernel's average launch duration in the
+    #     running workload (world == 1; with TP the phase also holds the all-reduces)
+    phase = None
+    if world == 1:
+        try:
+            pev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+            gp = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gp, stream=stream):
+                st.run(phase_events=pev)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    gp.replay()
+            torch.cuda.synchronize()
+            g_ms, h_ms = [], []
+            for _ in range(max(5, min(args.steps, 40))):
+                with torch.cuda.stream(stream):
+                    gp.replay()
+                torch.cuda.synchronize()
+                g_ms.append(pev[0].elapsed_time(pev[1]))
+                h_ms.append(pev[1].elapsed_time(pev[2]))
+            del gp
+            phase = (statistics.median(g_ms), statistics.median(h_ms))
+        except Exception as e:  # noqa: BLE001
+            phase = None
+            print(f"phase timing failed: {e!r}", file=sys.stderr)
+    # (2) instrumented replay (events between launches, PDL off): per-GEMM breakdown, and the headline with TP
     roofline = None
     try:
         n_ev = st.launches_per_step + 1
@@ -358,12 +392,13 @@ def run_ours(args, rank: int, world: int, local: int):
             head_ms.append(d[-1])
         del g2
         n_gemm = st.launches_per_step - 1
-        per_launch_ms = statistics.median(gemm_ms) / n_gemm
+        iso_launch_ms = statistics.median(gemm_ms) / n_gemm
+        per_launch_ms = phase[0] / n_gemm if phase else iso_launch_ms
         gemm_bytes = sum(st.gemm_bytes(nm) for nm, *_ in LAYER) * args.layers / n_gemm
         peak, peak_src = peak_hbm()
         achieved = gemm_bytes / (per_launch_ms * 1e-3) / 1e9
         traffic, tsrc = traffic_from_profiles()
-        head_launch_ms = statistics.median(head_ms)
+        head_launch_ms = phase[1] if phase else statistics.median(head_ms)
         head_bytes = alg_bytes(st.head_n, HEAD[2], args.m, head=True)
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -371,7 +406,10 @@ def run_ours(args, rank: int, world: int, local: int):
                     "bytes_per_launch": round(gemm_bytes), "us_per_launch": round(per_launch_ms * 1e3, 3),
                     "peak_source": peak_src + ", 'of measured'", "frac_of_nominal_8TBs": round(achieved / NOMINAL_HBM_GBS, 4),
                     "traffic_source": tsrc,
-                    "timing": "CUDA events around every launch of a replay of the same step (PDL off), median of 5",
+                    "timing": ("decoder-GEMM phase of the step graph (PDL on) between CUDA events at the step start "
+                               "and after the last GEMM, / 256 launches, median over replays" if phase else
+                               "CUDA events around every launch of a replay of the same step (PDL off), median of 5"),
+                    "us_per_launch_isolated": round(iso_launch_ms * 1e3, 3),
                     "head": {"us": round(head_launch_ms * 1e3, 2),
                              "GBps": round(head_bytes / (head_launch_ms * 1e-3) / 1e9, 1),
                              "frac": round(head_bytes / (head_launch_ms * 1e-3) / 1e9 / peak, 4)},
@@ -381,7 +419,7 @@ def run_ours(args, rank: int, world: int, local: int):
         for j, (nm, *_r) in enumerate(LAYER):
             vals = d[j:n_gemm:len(LAYER)]
             us = statistics.median(vals) * 1e3
-            roofline["per_gemm_us"][nm] = {"us": round(us, 2),
+            roofline["per_gemm_us"][nm] = {"us_isolated": round(us, 2),
                                            "GBps": round(st.gemm_bytes(nm) / (us * 1e-6) / 1e9, 1)}
     except Exception as e:  # noqa: BLE001
         roofline = {"error": f"instrumented replay failed: {e!r}"}
