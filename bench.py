@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--m", type=int, default=5)
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--allreduce", choices=["nvlink", "nccl"], default="nvlink",
+                    help="row-parallel partial-sum all-reduce with TP > 1: the NVLink one-shot kernel or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
@@ -176,10 +178,14 @@ def run_reference(args, rank: int, world: int):
 class Step:
     """Weights, activation buffers and the launch sequence of one tensor-parallel decode step."""
 
-    def __init__(self, layers: int, M: int, rank: int, world: int, dev, pdl: bool):
+    def __init__(self, layers: int, M: int, rank: int, world: int, dev, pdl: bool, allreduce: str = "nvlink"):
         import torch
         self.torch = torch
         self.M, self.rank, self.world, self.dev, self.pdl = M, rank, world, dev, pdl
+        self.ar = None
+        if world > 1 and allreduce == "nvlink":
+            from qwen_a100_fastpath_b200.tp import NVLinkAllReduce
+            self.ar = NVLinkAllReduce(M * max(N for _, N, _, st in LAYER if st == "row"))
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
         self.layers = []
         for _ in range(layers):
@@ -238,7 +244,10 @@ class Step:
                     events[e].record()
                     e += 1
                 if style == "row" and self.world > 1:
-                    tp.all_reduce_partial(y)
+                    if self.ar is not None:
+                        self.ar(y, pdl=self.pdl)
+                    else:
+                        tp.all_reduce_partial(y)
         if phase_events is not None:
             phase_events[1].record()
         w, s = self.head_w
@@ -321,7 +330,7 @@ def run_ours(args, rank: int, world: int, local: int):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
     torch.backends.cuda.matmul.allow_tf32 = False
     pdl = not args.no_pdl
-    st = Step(args.layers, args.m, rank, world, dev, pdl)
+    st = Step(args.layers, args.m, rank, world, dev, pdl, args.allreduce)
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
@@ -466,6 +475,8 @@ def run_ours(args, rank: int, world: int, local: int):
     status = workspace_status(dev, stream)
     del graph
     if world > 1:
+        if st.ar is not None:
+            st.ar.close()
         barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -481,6 +492,8 @@ def run_ours(args, rank: int, world: int, local: int):
                        "m": args.m, "layers": args.layers, "tp": world, "parallelism": f"tp{world}",
                        "int8_weight_bytes": sum(N * K for _, N, K, _ in LAYER) * args.layers + HEAD[1] * HEAD[2],
                        "alg_bytes_per_step": total_bytes, "cuda_graph": True, "pdl": pdl,
+                       "allreduce": ("none" if world == 1 else "nvlink one-shot kernel (qf_allreduce_bf16)"
+                                     if st.ar is not None else "nccl"),
                        "l2": "no flush: each step streams 23.9 GB of weights through the 126 MB L2"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
             "gpu_launches": st.launches_per_step * args.steps,

@@ -107,6 +107,36 @@ int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t l
  * QF_OK or QF_ERR_TIMEOUT.  Not for the hot path. */
 int qf_workspace_status(void* ws, void* stream, int* status);
 
+/* ---- tensor parallelism: one-shot all-reduce over NVLink peer memory ----------------------------------------
+ * Replaces the NCCL all-reduce that vLLM issues after a row-parallel layer (o_proj, down) under tensor
+ * parallelism; the reference plugin has no code of its own here (it runs on one GPU and leaves the collective to
+ * vLLM's NCCL).  Every rank of one node allocates one symmetric buffer of qf_allreduce_buffer_bytes(max_count)
+ * bytes (qf_symm_alloc: zero-filled), exports it with qf_ipc_handle, opens the other ranks' buffers with
+ * qf_ipc_open (CUDA IPC; peers reached over NVLink), and passes all `world` buffer pointers (its own at [rank]) to
+ * every call.  Calls are collective: every rank makes the same sequence of calls with the same count.  The
+ * epoch bookkeeping lives in the buffer, so calls can be captured in CUDA graphs. */
+#define QF_AR_MAX_RANKS 8
+#define QF_AR_MAX_CHUNKS 256    /* count <= 256 * 1024 elements */
+#define QF_IPC_HANDLE_BYTES 64
+
+/* Bytes of one rank's symmetric buffer for vectors of up to max_count bf16 elements (0 if max_count <= 0). */
+size_t qf_allreduce_buffer_bytes(int max_count);
+/* cudaMalloc + zero fill (synchronous) of a buffer to be shared between ranks; qf_symm_free releases it. */
+int qf_symm_alloc(size_t bytes, void** dev_ptr);
+int qf_symm_free(void* dev_ptr);
+/* CUDA IPC handle (QF_IPC_HANDLE_BYTES bytes) of a qf_symm_alloc buffer; open / close another rank's buffer. */
+int qf_ipc_handle(void* dev_ptr, void* handle_out);
+int qf_ipc_open(const void* handle, void** peer_ptr);
+int qf_ipc_close(void* peer_ptr);
+/* out[i] = bf16( sum over ranks r = 0..world-1, in that order, of in_r[i] ), fp32 sums; identical on every rank.
+ * in / out: bf16 [count], 16-byte aligned, may alias; count and max_count multiples of 8, count <= max_count <=
+ * QF_AR_MAX_CHUNKS * 1024; bufs[r]: rank r's buffer (256-byte aligned).  Waits for the other ranks are bounded (2 s);
+ * an expired wait is recorded in the buffer (qf_allreduce_status).  flags: QF_FLAG_PDL. */
+int qf_allreduce_bf16(const void* in, void* out, int count, int max_count, int rank, int world,
+                      void* const* bufs, unsigned flags, void* stream);
+/* Reads and clears the sticky error word of this rank's buffer (synchronises `stream`). */
+int qf_allreduce_status(void* own_buf, void* stream, int* status);
+
 /* Static description of the error code. */
 const char* qf_strerror(int code);
 /* Message of the last failing call on this thread. */

@@ -18,6 +18,9 @@ QF_MAX_M = 16
 QF_MAX_N = 1048576
 QF_FLAG_PDL = 1
 QF_NOALLOC_MAX_N = 65536
+QF_AR_MAX_RANKS = 8
+QF_AR_MAX_CHUNKS = 256
+QF_IPC_HANDLE_BYTES = 64
 ABI_VERSION = 1
 
 # (name, restype, argtypes) -- one entry per function declared in include/qf_b200.h
@@ -35,6 +38,16 @@ SIGNATURES = [
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64,
       _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_uint, _c.c_void_p]),
     ("qf_workspace_status", _c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(_c.c_int)]),
+    ("qf_allreduce_buffer_bytes", _c.c_size_t, [_c.c_int]),
+    ("qf_symm_alloc", _c.c_int, [_c.c_size_t, _c.POINTER(_c.c_void_p)]),
+    ("qf_symm_free", _c.c_int, [_c.c_void_p]),
+    ("qf_ipc_handle", _c.c_int, [_c.c_void_p, _c.c_void_p]),
+    ("qf_ipc_open", _c.c_int, [_c.c_void_p, _c.POINTER(_c.c_void_p)]),
+    ("qf_ipc_close", _c.c_int, [_c.c_void_p]),
+    ("qf_allreduce_bf16", _c.c_int,
+     [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(_c.c_void_p), _c.c_uint,
+      _c.c_void_p]),
+    ("qf_allreduce_status", _c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(_c.c_int)]),
     ("qf_strerror", _c.c_char_p, [_c.c_int]),
     ("qf_last_error_detail", _c.c_char_p, []),
     ("qf_abi_version", _c.c_int, []),

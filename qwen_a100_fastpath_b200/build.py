@@ -16,7 +16,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIB = PKG / "libqf_b200.so"
-SOURCES = ["qf_w8a16.cu"]
+SOURCES = ["qf_w8a16.cu", "qf_allreduce.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -28,7 +28,8 @@ def nvcc_path() -> str:
 
 
 def _inputs() -> list[Path]:
-    return [CSRC / s for s in SOURCES] + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    return [CSRC / s for s in SOURCES] + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + \
+        sorted(INCLUDE.glob("*.h"))
 
 
 def needs_build() -> bool:

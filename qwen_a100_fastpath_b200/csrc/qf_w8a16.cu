@@ -47,6 +47,7 @@
 #include <string>
 
 #include "../../include/qf_b200.h"
+#include "qf_host.h"
 #include "qf_ptx.cuh"
 
 namespace qf {
@@ -903,14 +904,15 @@ __global__ void fill_empty_k_kernel(const Params p) {
 }
 
 // ================================================================================== host side
-namespace {
-
 thread_local std::string g_err;
 
+// Records the message behind a failing entry point (qf_last_error_detail) and returns its code.
 int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
 }
+
+namespace {
 
 struct DeviceInfo {
   int ok = 0;             // 1 = checked and sm_100, -1 = wrong arch

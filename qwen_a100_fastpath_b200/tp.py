@@ -47,9 +47,84 @@ def shard_activations(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
 
 
 def all_reduce_partial(y: torch.Tensor, group=None) -> torch.Tensor:
-    """Sum the row-parallel partial outputs of all ranks in place (NCCL on GPUs, gloo on CPU)."""
+    """Sum the row-parallel partial outputs of all ranks in place with torch.distributed (NCCL on GPUs, gloo on
+    CPU): the collective vLLM issues after RowParallelLinear, kept as the comparison path."""
     dist.all_reduce(y, group=group)
     return y
+
+
+class NVLinkAllReduce:
+    """One-shot all-reduce of bf16 tensors between the ranks of one node over NVLink peer memory
+    (``qf_allreduce_bf16``): the replacement for the NCCL all-reduce after the row-parallel layers.
+
+    Collective construction: every rank allocates a symmetric buffer for vectors of up to ``max_count`` elements,
+    the CUDA IPC handles are exchanged with ``all_gather_object`` and every rank opens the others' buffers. Calls
+    are collective too (same sequence and sizes on every rank); the result is bit-identical on all ranks (fp32 sums
+    in rank order, one bf16 rounding) and the call can be captured in a CUDA graph."""
+
+    def __init__(self, max_count: int, group=None):
+        import ctypes
+
+        from ._lib import LIB, QF_AR_MAX_RANKS, QF_IPC_HANDLE_BYTES, check
+        self._lib, self._check, self._ct = LIB, check, ctypes
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > QF_AR_MAX_RANKS:
+            raise ValueError(f"at most {QF_AR_MAX_RANKS} ranks")
+        self.max_count = (int(max_count) + 7) // 8 * 8
+        ptr = ctypes.c_void_p()
+        check("qf_symm_alloc", LIB.qf_symm_alloc(LIB.qf_allreduce_buffer_bytes(self.max_count), ctypes.byref(ptr)))
+        self.own = ptr.value
+        handle = (ctypes.c_char * QF_IPC_HANDLE_BYTES)()
+        check("qf_ipc_handle", LIB.qf_ipc_handle(self.own, handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        bufs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bufs.append(self.own)
+                continue
+            pp = ctypes.c_void_p()
+            check("qf_ipc_open", LIB.qf_ipc_open(h, ctypes.byref(pp)))
+            self._opened.append(pp.value)
+            bufs.append(pp.value)
+        self._bufs = (ctypes.c_void_p * self.world)(*bufs)
+        dist.barrier(group)
+
+    def __call__(self, t: torch.Tensor, out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+        """Sum ``t`` over the ranks into ``out`` (default: in place) on the current stream."""
+        from ._lib import QF_FLAG_PDL
+        if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("NVLinkAllReduce needs a contiguous bf16 CUDA tensor")
+        if t.numel() > self.max_count or t.numel() % 8:
+            raise ValueError(f"numel {t.numel()} must be a multiple of 8 and <= {self.max_count}")
+        out = t if out is None else out
+        stream = torch.cuda.current_stream(t.device).cuda_stream
+        self._check("qf_allreduce_bf16", self._lib.qf_allreduce_bf16(
+            t.data_ptr(), out.data_ptr(), t.numel(), self.max_count, self.rank, self.world, self._bufs,
+            QF_FLAG_PDL if pdl else 0, stream))
+        return out
+
+    def status(self) -> int:
+        """Sticky device error word of this rank's buffer (0 or QF_ERR_TIMEOUT), cleared on read; synchronises."""
+        st = self._ct.c_int(0)
+        self._check("qf_allreduce_status", self._lib.qf_allreduce_status(
+            self.own, torch.cuda.current_stream().cuda_stream, self._ct.byref(st)))
+        return st.value
+
+    def close(self) -> None:
+        """Collective: unmap the other ranks' buffers, wait for every rank, free this rank's buffer."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        for pp in self._opened:
+            self._check("qf_ipc_close", self._lib.qf_ipc_close(pp))
+        self._opened = []
+        dist.barrier(self.group)
+        self._check("qf_symm_free", self._lib.qf_symm_free(self.own))
+        self.own = None
 
 
 def pack_head_stats(row_max: torch.Tensor, row_argmax: torch.Tensor, row_lse: torch.Tensor) -> torch.Tensor:

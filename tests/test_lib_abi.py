@@ -97,3 +97,34 @@ def test_head_argument_validation():
     k0 = list(args)
     k0[9] = 0
     assert f(*k0) == -2
+
+
+def allreduce(**kw):
+    bufs = (ctypes.c_void_p * 8)(*([FAKE] * 8))
+    a = dict(inp=FAKE, out=FAKE, count=5 * 5120, max_count=16 * 5120, rank=0, world=2, bufs=bufs, flags=0,
+             stream=None)
+    a.update(kw)
+    return _lib.LIB.qf_allreduce_bf16(*a.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(world=0), -1),
+    (dict(world=9), -1),
+    (dict(rank=2), -1),
+    (dict(count=16 * 5120 + 8), -2),           # above max_count
+    (dict(count=12), -2),                      # not a multiple of 8
+    (dict(max_count=256 * 1024 + 8), -2),      # above QF_AR_MAX_CHUNKS * 1024
+    (dict(inp=FAKE + 8), -4),
+    (dict(out=None), -1),
+])
+def test_allreduce_argument_validation(kw, code):
+    assert allreduce(**kw) == code
+    assert len(_lib.LIB.qf_last_error_detail()) > 0
+
+
+def test_allreduce_empty_and_buffer_size():
+    assert allreduce(count=0) == 0
+    assert _lib.LIB.qf_allreduce_buffer_bytes(0) == 0
+    small = _lib.LIB.qf_allreduce_buffer_bytes(8)
+    big = _lib.LIB.qf_allreduce_buffer_bytes(16 * 5120)
+    assert big - small == (16 * 5120 - 8) * 2 * 2 * _lib.QF_AR_MAX_RANKS   # bf16 x 2 parities x 8 source slots
