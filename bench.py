@@ -60,8 +60,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--m", type=int, default=5)
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--allreduce", choices=["nvlink", "nccl"], default="nvlink",
-                    help="row-parallel partial-sum all-reduce with TP > 1: the NVLink one-shot kernel or NCCL")
+    ap.add_argument("--allreduce", choices=["fused", "nvlink", "nccl"], default="fused",
+                    help="row-parallel partial-sum all-reduce with TP > 1: fused into the GEMM epilogue over NVLink, "
+                         "the standalone NVLink one-shot kernel, or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
@@ -183,7 +184,8 @@ class Step:
         self.torch = torch
         self.M, self.rank, self.world, self.dev, self.pdl = M, rank, world, dev, pdl
         self.ar = None
-        if world > 1 and allreduce == "nvlink":
+        self.fused = world > 1 and allreduce == "fused"
+        if world > 1 and allreduce in ("nvlink", "fused"):
             from qwen_a100_fastpath_b200.tp import NVLinkAllReduce
             self.ar = NVLinkAllReduce(M * max(N for _, N, _, st in LAYER if st == "row"))
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
@@ -227,7 +229,7 @@ class Step:
         ``phase_events`` records three events: step start, after the last decoder GEMM, after the head."""
         torch = self.torch
         from qwen_a100_fastpath_b200 import tp
-        from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_mm
+        from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_mm, w8a16_mm_allreduce
         if events is not None:
             events[0].record()
         if phase_events is not None:
@@ -236,14 +238,18 @@ class Step:
         for ws in self.layers:
             for name, _, _, style in LAYER:
                 w, s = ws[name]
-                if linear is None:
+                fused_row = self.fused and style == "row"
+                if fused_row:  # row-parallel GEMM with the all-reduce in its epilogue
+                    y = w8a16_mm_allreduce(self.x[name], w, s, self.ar, out=None if linear else self.y[name],
+                                           pdl=self.pdl)
+                elif linear is None:
                     y = w8a16_mm(self.x[name], w, s, None, torch.bfloat16, out=self.y[name], pdl=self.pdl)
                 else:
                     y = linear(self.x[name], w, s)
                 if events is not None:
                     events[e].record()
                     e += 1
-                if style == "row" and self.world > 1:
+                if style == "row" and self.world > 1 and not fused_row:
                     if self.ar is not None:
                         self.ar(y, pdl=self.pdl)
                     else:
@@ -492,7 +498,9 @@ def run_ours(args, rank: int, world: int, local: int):
                        "m": args.m, "layers": args.layers, "tp": world, "parallelism": f"tp{world}",
                        "int8_weight_bytes": sum(N * K for _, N, K, _ in LAYER) * args.layers + HEAD[1] * HEAD[2],
                        "alg_bytes_per_step": total_bytes, "cuda_graph": True, "pdl": pdl,
-                       "allreduce": ("none" if world == 1 else "nvlink one-shot kernel (qf_allreduce_bf16)"
+                       "allreduce": ("none" if world == 1 else
+                                     "fused into the row-parallel GEMM epilogue over NVLink (qf_w8a16_gemm_allreduce)"
+                                     if st.fused else "nvlink one-shot kernel (qf_allreduce_bf16)"
                                      if st.ar is not None else "nccl"),
                        "l2": "no flush: each step streams 23.9 GB of weights through the 126 MB L2"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,

@@ -137,6 +137,18 @@ int qf_allreduce_bf16(const void* in, void* out, int count, int max_count, int r
 /* Reads and clears the sticky error word of this rank's buffer (synchronises `stream`). */
 int qf_allreduce_status(void* own_buf, void* stream, int* status);
 
+/* Row-parallel W8A16 GEMM with the all-reduce fused into its epilogue: y = bf16( sum over ranks r, in rank order, of
+ * bf16(scale * x_r . w_r) ) on every rank, where each rank holds its K-shard of x and w (vLLM's RowParallelLinear
+ * followed by its NCCL all-reduce; no counterpart in the reference plugin).  Each finished output tile is pushed to
+ * every rank's buffer over NVLink and summed as soon as all ranks' copies of that tile have arrived, so the
+ * collective overlaps the GEMM's remaining tiles.  Collective: every rank calls it with the same M, N and K.
+ * Arguments as qf_w8a16_gemm (bf16 output only, no bias) plus the qf_allreduce_bf16 buffers (bufs, max_count,
+ * same buffers and epoch sequence: the two calls may be mixed on one set of buffers).  max_count must hold the
+ * output with its tiles rounded up (N rounded up to 128, times M); at most QF_AR_MAX_CHUNKS output tiles. */
+int qf_w8a16_gemm_allreduce(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
+                            void* y, int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes,
+                            int rank, int world, void* const* bufs, int max_count, unsigned flags, void* stream);
+
 /* Static description of the error code. */
 const char* qf_strerror(int code);
 /* Message of the last failing call on this thread. */

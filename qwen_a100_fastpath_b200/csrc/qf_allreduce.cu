@@ -26,6 +26,7 @@
 #include <string>
 
 #include "../../include/qf_b200.h"
+#include "qf_comm.cuh"
 #include "qf_host.h"
 #include "qf_ptx.cuh"
 
@@ -34,12 +35,6 @@ namespace {
 
 constexpr int kArThreads = 128;
 constexpr int kArChunk = 1024;                  // bf16 elements per CTA
-constexpr uint64_t kArWaitNs = 2000000000ull;   // 2 s
-// buffer layout (bytes)
-constexpr size_t kArHeader = 256;               // u32 [0] error flag, [1] epoch, [2] CTAs done
-constexpr size_t kArFlags = kArHeader;          // u32 flags[2 parity][QF_AR_MAX_RANKS src][QF_AR_MAX_CHUNKS]
-constexpr size_t kArData = kArFlags + sizeof(uint32_t) * 2 * QF_AR_MAX_RANKS * QF_AR_MAX_CHUNKS;
-static_assert(kArData % 256 == 0, "data alignment");
 
 struct ArParams {
   const __nv_bfloat16* in;
@@ -51,16 +46,12 @@ struct ArParams {
   uint8_t* bufs[QF_AR_MAX_RANKS];  // every rank's buffer, this rank's at [rank]
 };
 
-__device__ __forceinline__ uint4* slot_ptr(uint8_t* buf, int par, int src, int max_count, int e0) {
-  return reinterpret_cast<uint4*>(buf + kArData +
-                                  (static_cast<size_t>(par * QF_AR_MAX_RANKS + src) * max_count + e0) * 2);
-}
-__device__ __forceinline__ uint32_t* flag_ptr(uint8_t* buf, int par, int src, int chunk) {
-  return reinterpret_cast<uint32_t*>(buf + kArFlags) + (par * QF_AR_MAX_RANKS + src) * QF_AR_MAX_CHUNKS + chunk;
-}
 
 __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p) {
-  pdl_wait();  // the input is the previous kernel's output
+  // The next kernel may be scheduled now (its weight prefetch overlaps this kernel; it reads this kernel's
+  // output only after its own griddepcontrol.wait).  The input is the previous kernel's output.
+  pdl_launch_dependents();
+  pdl_wait();
   uint8_t* own = p.bufs[p.rank];
   uint32_t* hdr = reinterpret_cast<uint32_t*>(own);
   __shared__ uint32_t s_epoch;
@@ -80,17 +71,15 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p)
   const uint4* src = reinterpret_cast<const uint4*>(p.in + e0);
   for (int i = threadIdx.x; i < nv; i += kArThreads) {
     const uint4 v = src[i];
-    for (int r = 0; r < p.world; ++r) slot_ptr(p.bufs[r], par, p.rank, p.max_count, e0)[i] = v;
+    for (int r = 0; r < p.world; ++r) ar_slot(p.bufs[r], par, p.rank, p.max_count, e0)[i] = v;
   }
   __syncthreads();
-  // 2. publish: thread r makes the CTA's stores visible system-wide, then raises flag [rank][c] on rank r
-  if (threadIdx.x < p.world) {
-    __threadfence_system();
-    st_release_sys(flag_ptr(p.bufs[threadIdx.x], par, p.rank, c), epoch);
-  }
+  // 2. publish: after the CTA barrier, thread r raises flag [rank][c] on rank r with a system-scope release,
+  //    which orders the whole CTA's stores above before the flag
+  if (threadIdx.x < p.world) st_release_sys(ar_flag(p.bufs[threadIdx.x], par, p.rank, c), epoch);
   // 3. wait for every rank's chunk c (flags only grow: a stale value is epoch - 2)
   if (threadIdx.x < p.world) {
-    const uint32_t* f = flag_ptr(own, par, threadIdx.x, c);
+    const uint32_t* f = ar_flag(own, par, threadIdx.x, c);
     if (ld_acquire_sys(f) != epoch) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_sys(f) != epoch) {
@@ -109,7 +98,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p)
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[k] = 0.f;
     for (int r = 0; r < p.world; ++r) {
-      const uint4 v = __ldcg(slot_ptr(own, par, r, p.max_count, e0) + i);
+      const uint4 v = __ldcg(ar_slot(own, par, r, p.max_count, e0) + i);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {

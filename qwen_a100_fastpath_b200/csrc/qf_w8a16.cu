@@ -47,6 +47,7 @@
 #include <string>
 
 #include "../../include/qf_b200.h"
+#include "qf_comm.cuh"
 #include "qf_host.h"
 #include "qf_ptx.cuh"
 
@@ -123,6 +124,9 @@ struct Params {
   int f16_path;
   uint32_t x_tx;  // activation bytes per stage: 2 B boxes of M rows x 128 bytes
   int out_vec;     // bf16 output rows (y or logits) can be written with 16-byte stores
+  // fused all-reduce of y over the tensor-parallel ranks (row-parallel layers); ar_world == 0: off
+  int ar_world, ar_rank, ar_max_count;
+  uint8_t* ar_bufs[QF_AR_MAX_RANKS];
   // head
   __nv_bfloat16* logits;
   int64_t ldl;
@@ -273,12 +277,85 @@ __device__ __forceinline__ MaxArg ma_shfl_xor(const MaxArg& v, int mask) {
   return MaxArg{__shfl_xor_sync(0xffffffffu, v.m, mask), __shfl_xor_sync(0xffffffffu, v.a, mask)};
 }
 
+// Fused all-reduce of one finished output tile (bf16 rows staged in sOut, [M][BN + 8]) by the epilogue warp:
+// push the tile into slot [rank] of every rank's symmetric buffer (peer stores over NVLink; the tile occupies
+// elements [tile*BN*M, (tile+1)*BN*M) of a slot, token-major), raise flag [rank][tile] on every rank
+// (system-scope release), wait (bounded) for every rank's flag [*][tile] in this rank's buffer, then sum the ranks'
+// tiles in rank order in fp32, round once to bf16 and store the rows of y.  Every rank computes the same bits.
+template <int BN>
+__device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int lane, const __nv_bfloat16* sOut,
+                                                  uint32_t epoch) {
+  constexpr int OS = BN + 8;
+  constexpr int TV = BN / 8;  // 16-byte vectors per token row of the tile
+  const int par = static_cast<int>(epoch & 1u);
+  const int nvec = p.M * TV;
+  const int e0 = tile * BN * p.M;
+  for (int r = 0; r < p.ar_world; ++r) {
+    uint4* dst = ar_slot(p.ar_bufs[r], par, p.ar_rank, p.ar_max_count, e0);
+    for (int idx = lane; idx < nvec; idx += 32) {
+      const int m = idx / TV;
+      dst[idx] = *reinterpret_cast<const uint4*>(sOut + m * OS + (idx - m * TV) * 8);
+    }
+  }
+  __syncwarp();  // every lane's stores precede the releases below
+  uint8_t* own = p.ar_bufs[p.ar_rank];
+  if (lane < p.ar_world) st_release_sys(ar_flag(p.ar_bufs[lane], par, p.ar_rank, tile), epoch);
+  int timed_out = 0;
+  if (lane < p.ar_world) {
+    const uint32_t* f = ar_flag(own, par, lane, tile);
+    if (ld_acquire_sys(f) != epoch) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(f) != epoch) {
+        if (global_timer_ns() - t0 > kArWaitNs) {
+          timed_out = 1;
+          break;
+        }
+      }
+    }
+  }
+  if (__any_sync(0xffffffffu, timed_out) && lane == 0)
+    atomicExch(reinterpret_cast<uint32_t*>(own), static_cast<uint32_t>(QF_ERR_TIMEOUT));
+  __syncwarp();  // the acquiring lanes' view covers the other lanes' loads below
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+  for (int idx = lane; idx < nvec; idx += 32) {
+    const int m = idx / TV;
+    const int n = tile * BN + (idx - m * TV) * 8;
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    for (int r = 0; r < p.ar_world; ++r) {
+      const uint4 v = __ldcg(ar_slot(own, par, r, p.ar_max_count, e0) + idx);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc[2 * k] += __uint_as_float(w[k] << 16);
+        acc[2 * k + 1] += __uint_as_float(w[k] & 0xFFFF0000u);
+      }
+    }
+    __nv_bfloat16* out = y + static_cast<int64_t>(m) * p.ldy + n;
+    if (p.out_vec && n + 8 <= p.N) {
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+        ow[k] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+      *reinterpret_cast<uint4*>(out) = o;
+    } else {
+      for (int k = 0; k < 8; ++k)
+        if (n + k < p.N) out[k] = __float2bfloat16_rn(acc[k]);
+    }
+  }
+}
+
 // Reduction of a stream-K tile from every contributor's slot (CTAs c_first .. c_last, in that order), by the
 // contributor that arrived last when the tile's designated reducer did not wait for the others: finishes the tile
 // (scale + store, or logits + tile statistics for the head) and re-arms the tile's counter.
-template <int BN, int NT, bool HEAD>
+template <int BN, int NT, bool HEAD, bool AR>
 __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int lane, int c_first, int c_last,
-                                                 int* counters, const float* partials, float4* sTile) {
+                                                 int* counters, const float* partials, float4* sTile,
+                                                 __nv_bfloat16* sOut, uint32_t ar_epoch) {
   // Slot = [BN rows][8*NT tokens] fp32, read as float4: lane takes float4 f = lane + 32 j (row f / (2 NT),
   // tokens 4 (lane % (2 NT)) + 0..3).  All of a contributor's loads (and those of U contributors) are issued
   // before they are added, in ascending CTA order.
@@ -327,7 +404,10 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
       for (int e = 0; e < 4; ++e) {
         const int m = m_base + e;
         if constexpr (!HEAD) {
-          store_out(p, n, m, vv[e] * sc);
+          if constexpr (AR)  // staged like finish_tile, published below
+            sOut[m * (BN + 8) + (lane + 32 * (pass * PC + j)) / (2 * NT)] = __float2bfloat16_rn(vv[e] * sc);
+          else
+            store_out(p, n, m, vv[e] * sc);
         } else {
           const __nv_bfloat16 rv = __float2bfloat16_rn(vv[e] * sc);
           if (p.logits && m < p.M && n < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n] = rv;
@@ -348,6 +428,10 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
         sTile[m_base + e] = make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
     }
   }
+  if constexpr (AR) {
+    __syncwarp();
+    ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch);
+  }
   if (lane == 0) counters[tile] = 0;  // ready for the next call on this workspace
 }
 
@@ -355,9 +439,10 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
 // tokens 8 nt + 2 t and 8 nt + 2 t + 1): scale, bf16 rounding (+ the bias as a second rounding), rows staged in
 // shared memory and written with 16-byte stores (GEMM output or head logits), and for the head the tile's per-token
 // (max, first argmax, sum exp) of its bf16 logits.
-template <int BN, int NT, bool HEAD>
+template <int BN, int NT, bool HEAD, bool AR>
 __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane, const float (&v)[BN / 16][NT][4],
-                                            const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* sTile) {
+                                            const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* sTile,
+                                            uint32_t ar_epoch) {
   constexpr int MT = BN / 16;
   constexpr int OS = BN + 8;
   const int g = lane >> 2;
@@ -418,7 +503,9 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
   __syncwarp();
   __nv_bfloat16* dst = HEAD ? p.logits : static_cast<__nv_bfloat16*>(p.y);
   const int64_t ld = HEAD ? p.ldl : p.ldy;
-  if (dst) {
+  if constexpr (AR) {
+    ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch);
+  } else if (dst) {
     constexpr int CH = BN / 8;
     for (int idx = lane; idx < p.M * CH; idx += 32) {
       const int m = idx / CH;
@@ -493,10 +580,11 @@ __device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTi
   __syncwarp();
 }
 
-template <int BN, int NT, int KS, bool HEAD>
+template <int BN, int NT, int KS, bool HEAD, bool AR>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  const Params p) {
+  static_assert(!(HEAD && AR), "the head is vocab-parallel: no all-reduce");
   using C = Geo<BN, NT, KS>;
   constexpr int S = C::kStages;
   constexpr int B = C::B;
@@ -639,6 +727,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         else tc = tt;
       }
     }
+    uint32_t ar_epoch = 0;  // fused all-reduce: this call's epoch (previous calls on these buffers + 1)
+    if constexpr (AR) {
+      uint32_t e = 0;
+      if (lane == 0) e = *reinterpret_cast<volatile uint32_t*>(p.ar_bufs[p.ar_rank] + 4) + 1u;
+      ar_epoch = __shfl_sync(0xffffffffu, e, 0);
+    }
     StageIter et = it;
     int tcount = 0;
     RowStat run{-INFINITY, INT_MAX, 0.f};  // head: lane m folds token m's statistics over this CTA's tiles
@@ -748,13 +842,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                  static_cast<uint32_t>(c_last - c_first);
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          split_reduce_all<BN, NT, HEAD>(p, tile, lane, c_first, c_last, counters, partials, sStat);
+          split_reduce_all<BN, NT, HEAD, AR>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut, ar_epoch);
           if constexpr (HEAD) fold_tile(p, lane, sStat, run);
         }
         continue;
       }
-      finish_tile<BN, NT, HEAD>(p, tile, lane, v, sc, sOut, sStat);
+      finish_tile<BN, NT, HEAD, AR>(p, tile, lane, v, sc, sOut, sStat, ar_epoch);
       if constexpr (HEAD) fold_tile(p, lane, sStat, run);
+    }
+    if (AR && lane == 0) {  // the last CTA to finish advances the buffers' epoch for the next call
+      uint32_t* hdr = reinterpret_cast<uint32_t*>(p.ar_bufs[p.ar_rank]);
+      if (atomicAdd(hdr + 2, 1u) == static_cast<uint32_t>(p.G - 1)) {
+        hdr[2] = 0u;
+        hdr[1] = ar_epoch;
+      }
     }
     if constexpr (HEAD) {
       if (lane < p.M) cta_stats[lane * kMaxGrid + cta] = make_float4(run.m, __int_as_float(run.a), run.s, 0.f);
@@ -1008,11 +1109,11 @@ void pick_tiles(int N, int K, int sms, int* bn, int* ks) {
   }
 }
 
-template <int BN, int NT, int KS, bool HEAD>
+template <int BN, int NT, int KS, bool HEAD, bool AR>
 int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
            unsigned flags, cudaStream_t stream) {
   using C = Geo<BN, NT, KS>;
-  auto kern = w8a16_kernel<BN, NT, KS, HEAD>;
+  auto kern = w8a16_kernel<BN, NT, KS, HEAD, AR>;
   static bool smem_attr_set[64] = {};
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -1037,6 +1138,9 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   p.kiters = (p.K + KS - 1) / KS;
   p.ntiles = (p.N + BN - 1) / BN;
   if (p.ntiles > kMaxTiles) return fail(QF_ERR_SHAPE, "too many tiles for this tile height");
+  if (p.ar_world && (p.ntiles > QF_AR_MAX_CHUNKS || static_cast<long long>(p.ntiles) * BN * p.M > p.ar_max_count))
+    return fail(QF_ERR_SHAPE, "output too large for the all-reduce buffers (max_count) or more than "
+                              "QF_AR_MAX_CHUNKS tiles");
   const long long total = static_cast<long long>(p.kiters) * p.ntiles;
   int G = dinfo->sm_count;
   if (G > kMaxGrid) G = kMaxGrid;
@@ -1068,11 +1172,11 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   return QF_OK;
 }
 
-template <int BN, int KS, bool HEAD>
+template <int BN, int KS, bool HEAD, bool AR>
 int launch_nt(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
               unsigned flags, cudaStream_t st) {
-  if (p.M <= 8) return launch<BN, 1, KS, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  return launch<BN, 2, KS, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (p.M <= 8) return launch<BN, 1, KS, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  return launch<BN, 2, KS, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
 // Optional fixed tile shape (environment QF_TILES="BN:KS", read once; 0 = the per-shape choice): used by the
@@ -1091,17 +1195,17 @@ const TileShape& tile_override() {
   return v;
 }
 
-template <bool HEAD>
+template <bool HEAD, bool AR = false>
 int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
                unsigned flags, cudaStream_t st) {
   int bn = tile_override().bn, ks = tile_override().ks;
   if (bn == 0) pick_tiles(p.N, p.K, dinfo->sm_count, &bn, &ks);
-  if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 64 && ks == 512) return launch_nt<64, 512, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 32 && ks == 512) return launch_nt<32, 512, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 32 && ks == 1024) return launch_nt<32, 1024, HEAD>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 512) return launch_nt<64, 512, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 512) return launch_nt<32, 512, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 1024) return launch_nt<32, 1024, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
   return fail(QF_ERR_SHAPE, "no kernel instance for the chosen tile shape");
 }
 
@@ -1171,6 +1275,41 @@ int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
   return launch_any<false>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+}
+
+int qf_w8a16_gemm_allreduce(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,
+                            int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, int rank, int world,
+                            void* const* bufs, int max_count, unsigned flags, void* stream) {
+  int rc = check_common(x, ldx, w, ldw, scale, M, N, K, ws, ws_bytes);
+  if (rc) return rc;
+  if (world < 1 || world > QF_AR_MAX_RANKS) return fail(QF_ERR_INVALID, "world size must be 1..8");
+  if (rank < 0 || rank >= world) return fail(QF_ERR_INVALID, "rank out of range");
+  if (max_count <= 0 || max_count % 8) return fail(QF_ERR_SHAPE, "max_count must be a positive multiple of 8");
+  if (M == 0 || N == 0) return QF_OK;
+  if (K == 0) return fail(QF_ERR_SHAPE, "the fused all-reduce needs K >= 1");
+  if (!y || !bufs) return fail(QF_ERR_INVALID, "null y or buffer list");
+  if (M > 1 && ldy < N) return fail(QF_ERR_STRIDE, "ldy < N");
+  for (int r = 0; r < world; ++r)
+    if (!bufs[r] || reinterpret_cast<uintptr_t>(bufs[r]) % 256)
+      return fail(QF_ERR_ALIGN, "buffers must be non-null and 256-byte aligned");
+  int dev;
+  DeviceInfo* dinfo;
+  rc = device_info(&dev, &dinfo);
+  if (rc) return rc;
+  Params p = {};
+  p.scale = scale;
+  p.y = y;
+  p.ldy = ldy;
+  p.out_vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (M == 1 || ldy % 8 == 0);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ws = static_cast<uint8_t*>(ws);
+  p.ar_world = world;
+  p.ar_rank = rank;
+  p.ar_max_count = max_count;
+  for (int r = 0; r < world; ++r) p.ar_bufs[r] = static_cast<uint8_t*>(bufs[r]);
+  return launch_any<false, true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
 }
 
 int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* logits,

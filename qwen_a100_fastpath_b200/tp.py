@@ -93,6 +93,11 @@ class NVLinkAllReduce:
         self._bufs = (ctypes.c_void_p * self.world)(*bufs)
         dist.barrier(group)
 
+    @property
+    def buffer_list(self):
+        """ctypes array of every rank's buffer pointer (this rank's own at [rank]), for the C ABI."""
+        return self._bufs
+
     def __call__(self, t: torch.Tensor, out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
         """Sum ``t`` over the ranks into ``out`` (default: in place) on the current stream."""
         from ._lib import QF_FLAG_PDL

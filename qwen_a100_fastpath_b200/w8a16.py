@@ -156,6 +156,40 @@ def w8a16_mm(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, cfg=None
     return out
 
 
+def w8a16_mm_allreduce(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, comm, out: torch.Tensor | None = None,
+                       pdl: bool | None = None) -> torch.Tensor:
+    """Row-parallel layer with its all-reduce fused into the GEMM (``qf_w8a16_gemm_allreduce``): this rank holds the
+    K-shard ``x [M, K_r]`` / ``w_t [K_r, N]``; the result ``[M, N]`` bf16 is the rank-order fp32 sum of every rank's
+    bf16 partial, identical on all ranks (vLLM's RowParallelLinear + all-reduce).  ``comm`` is the
+    ``tp.NVLinkAllReduce`` that owns the ranks' symmetric buffers.  Collective: every rank calls it with the same
+    shapes."""
+    if x.dim() != 2 or w_t.shape[0] != x.shape[1]:
+        raise ValueError("x must be [M, K] matching w_t [K, N]")
+    M, K = x.shape
+    N = w_t.shape[1]
+    if M > SMALL_M or K < 1:
+        raise ValueError(f"need 1 <= K and M <= {SMALL_M}")
+    if not (x.is_cuda and w_t.is_cuda and w_scale.is_cuda) or x.dtype != torch.bfloat16:
+        raise ValueError("libqf_b200 needs CUDA tensors and bf16 activations (there is no CPU path)")
+    scale = w_scale.reshape(-1).contiguous()
+    if scale.numel() != N or scale.dtype != torch.float32:
+        raise ValueError("w_scale must hold N fp32 per-channel scales")
+    ldw = _check_weight(w_t, K)
+    x = _aligned_rows(x)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    elif out.shape != (M, N) or out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError("out must be bf16 [M, N] with unit column stride")
+    stream = torch.cuda.current_stream(x.device)
+    ws = workspace(x.device, stream, LIB.qf_w8a16_workspace_bytes(M, N, K))
+    flags = _lib.QF_FLAG_PDL if (_PDL_DEFAULT if pdl is None else pdl) else 0
+    rc = LIB.qf_w8a16_gemm_allreduce(x.data_ptr(), x.stride(0), w_t.data_ptr(), ldw, scale.data_ptr(), out.data_ptr(),
+                                     out.stride(0), M, N, K, ws.data_ptr(), ws.numel(), comm.rank, comm.world,
+                                     comm.buffer_list, comm.max_count, flags, stream.cuda_stream)
+    check("qf_w8a16_gemm_allreduce", rc)
+    return out
+
+
 def w8a16_head(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, n_valid: int | None = None,
                vocab_offset: int = 0, want_logits: bool = True, pdl: bool | None = None, out=None):
     """Int8 draft LM head: bf16 logits ``[M, N]`` (or ``None``) and per-row statistics over columns

@@ -1,6 +1,8 @@
 """Run under torchrun (one process per GPU, NCCL for the plumbing) or as one process with world size 1:
 NVLinkAllReduce (qf_allreduce_bf16) against the fp32 rank-order sum of every rank's input, eager and inside a
-CUDA graph, for the decode sizes M x 5120 (M = 1, 5, 16).  Exits non-zero on a mismatch.  Used by
+CUDA graph, for the decode sizes M x 5120 (M = 1, 5, 16); and the row-parallel GEMM with the fused all-reduce
+(qf_w8a16_gemm_allreduce) against the rank-order sum of every rank's partial computed by the plain GEMM kernel
+(the same accumulation, so the comparison is bit-exact).  Exits non-zero on a mismatch.  Used by
 test_gpu_tp.py."""
 from __future__ import annotations
 
@@ -22,6 +24,62 @@ def reference(xs: list[torch.Tensor]) -> torch.Tensor:
     for x in xs:  # rank order, fp32
         acc += x.float()
     return acc.to(torch.bfloat16)
+
+
+def shard(seed: int, M: int, N: int, K: int, dev):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+    return x, w
+
+
+def fused_cases(ar, rank: int, world: int, dev, stream) -> int:
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_mm, w8a16_mm_allreduce
+    bad = 0
+    N = 5120
+    scale = torch.rand(N, device=dev, generator=torch.Generator(device=dev).manual_seed(9)) * 0.009 + 0.001
+    for (K, M) in [(1024, 1), (2176, 5), (4352, 16), (8192, 5)]:
+        shards = [shard(1000 * K + 10 * M + r, M, N, K, dev) for r in range(world)]
+        partials = [w8a16_mm(x, w.t(), scale, None, torch.bfloat16) for x, w in shards]
+        want = reference(partials)
+        x, w = shards[rank]
+        y = w8a16_mm_allreduce(x, w.t(), scale, ar)
+        torch.cuda.synchronize()
+        if not torch.equal(y, want):
+            bad += 1
+            print(f"rank {rank}: fused mismatch K={K} M={M}: {(y != want).sum().item()} elements", flush=True)
+    # graph: fused GEMM, standalone all-reduce and fused GEMM again on the same buffers (one epoch sequence)
+    K, M = 2176, 5
+    shards = [shard(77 + r, M, N, K, dev) for r in range(world)]
+    x, w = shards[rank]
+    xs = x.clone()
+    y1 = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    y2 = torch.empty_like(y1)
+    with torch.cuda.stream(stream):
+        w8a16_mm_allreduce(xs, w.t(), scale, ar, out=y1, pdl=True)
+        ar(y1.view(-1), out=y2.view(-1), pdl=True)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        w8a16_mm_allreduce(xs, w.t(), scale, ar, out=y1, pdl=True)
+        ar(y1.view(-1), out=y2.view(-1), pdl=True)
+        w8a16_mm_allreduce(xs, w.t(), scale, ar, out=y1, pdl=True)
+    for rep in range(2):
+        shards = [shard(300 + 10 * rep + r, M, N, K, dev) for r in range(world)]
+        xs.copy_(shards[rank][0])
+        # every rank's weights stay those captured; only the activations change
+        partials = [w8a16_mm(shards[r][0], shard(77 + r, M, N, K, dev)[1].t(), scale, None, torch.bfloat16)
+                    for r in range(world)]
+        first = reference(partials)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            graph.replay()
+        torch.cuda.synchronize()
+        if not torch.equal(y1, first) or not torch.equal(y2, reference([first] * world)):
+            bad += 1
+            print(f"rank {rank}: fused graph mismatch rep={rep}", flush=True)
+    del graph
+    return bad
 
 
 def main() -> int:
@@ -74,6 +132,7 @@ def main() -> int:
             bad += 1
             print(f"rank {rank}: graph mismatch rep={rep}", flush=True)
     del graph
+    bad += fused_cases(ar, rank, world, dev, stream)
     status = ar.status()
     if status != 0:
         bad += 1
