@@ -4,20 +4,21 @@
 // Under tensor parallelism the row-parallel layers of the decode path (o_proj, down) end with a sum of every
 // rank's bf16 partial output [M, 5120]; vLLM issues an NCCL all-reduce for it after RowParallelLinear (the
 // reference plugin leaves that call to vLLM).  At decode sizes (M <= 16: at most 160 KB per rank) the all-reduce
-// is pure latency, so this kernel does it in one pass:
+// is pure latency, so this kernel does it in one pass with self-validating lines (qf_comm.cuh):
 //
 //   * every rank owns one symmetric buffer (cudaMalloc'd, shared with the other ranks through CUDA IPC);
-//   * CTA c of every rank takes elements [c*1024, (c+1)*1024): it stores its input chunk into slot [rank] of every
-//     rank's buffer (peer stores over NVLink), then sets flag [rank][c] in every rank's buffer to the call's
-//     epoch (st.release.sys);
-//   * it waits (bounded) until all ranks' flags [*][c] in its own buffer carry the epoch, then sums the W slots in
-//     rank order in fp32 and rounds once to bf16: every rank computes the same bits, deterministic.
+//   * CTA c of every rank takes elements [c*1024, (c+1)*1024): it writes its input chunk as lines
+//     {v0v1, epoch, v2v3, epoch} into slot [rank] of every other rank's buffer (peer stores over NVLink);
+//   * it then reads, for every element group, the other ranks' lines from its own buffer (spinning, bounded, until
+//     both halves carry the call's epoch) and sums all ranks' values in rank order in fp32, its own taken from its
+//     input, with one rounding to bf16: every rank computes the same bits, deterministic.
 //
+// No fence or flag round trip is needed: a line is valid exactly when both of its 8-byte halves carry the epoch.
 // Epochs live in device memory (the buffer header), so the call is CUDA-graph capturable: each launch reads
-// epoch = header.epoch + 1 and the last CTA to finish stores it back.  Slots and flags are double-buffered by
-// epoch parity: a rank can only reach epoch e + 2 after every rank has pushed epoch e + 1, i.e. finished reading
-// epoch e, so a slot is never overwritten while a peer still reads it.  A flag wait that exceeds kArWaitNs
-// records QF_ERR_TIMEOUT in the header (read by qf_allreduce_status) and the CTA continues.
+// epoch = header.epoch + 1 and the last CTA to finish stores it back.  Lines are double-buffered by epoch parity: a
+// rank reaches epoch e + 2 only after every rank has written its lines of epoch e + 1, i.e. finished reading epoch
+// e, so a line is never overwritten while a peer still reads it.  A wait that exceeds kArWaitNs records
+// QF_ERR_TIMEOUT in the header (read by qf_allreduce_status) and the CTA continues.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -63,61 +64,39 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p)
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const int par = static_cast<int>(epoch & 1u);
-  const int c = blockIdx.x;
-  const int e0 = c * kArChunk;
-  const int nv = min(kArChunk, p.count - e0) / 8;  // 16-byte vectors in this chunk
+  const int e0 = blockIdx.x * kArChunk;
+  const int nl = min(kArChunk, p.count - e0) / 4;  // lines (4 elements each) in this chunk
+  const uint2* src = reinterpret_cast<const uint2*>(p.in + e0);
 
-  // 1. push this rank's chunk into slot [rank] of every rank's buffer
-  const uint4* src = reinterpret_cast<const uint4*>(p.in + e0);
-  for (int i = threadIdx.x; i < nv; i += kArThreads) {
-    const uint4 v = src[i];
-    for (int r = 0; r < p.world; ++r) ar_slot(p.bufs[r], par, p.rank, p.max_count, e0)[i] = v;
+  // 1. write this rank's chunk as lines into slot [rank] of every other rank's buffer
+  for (int i = threadIdx.x; i < nl; i += kArThreads) {
+    const uint2 v = src[i];
+    const uint4 line = make_uint4(v.x, epoch, v.y, epoch);
+    for (int r = 0; r < p.world; ++r)
+      if (r != p.rank) st_volatile_v4(ar_line(p.bufs[r], par, p.rank, p.max_count, e0 / 4 + i), line);
   }
-  __syncthreads();
-  // 2. publish: after the CTA barrier, thread r raises flag [rank][c] on rank r with a system-scope release,
-  //    which orders the whole CTA's stores above before the flag
-  if (threadIdx.x < p.world) st_release_sys(ar_flag(p.bufs[threadIdx.x], par, p.rank, c), epoch);
-  // 3. wait for every rank's chunk c (flags only grow: a stale value is epoch - 2)
-  if (threadIdx.x < p.world) {
-    const uint32_t* f = ar_flag(own, par, threadIdx.x, c);
-    if (ld_acquire_sys(f) != epoch) {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(f) != epoch) {
-        if (global_timer_ns() - t0 > kArWaitNs) {
-          s_timeout = 1;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (s_timeout && threadIdx.x == 0) atomicExch(hdr, static_cast<uint32_t>(QF_ERR_TIMEOUT));
-  // 4. sum the ranks' slots in rank order (fp32), one rounding to bf16
-  for (int i = threadIdx.x; i < nv; i += kArThreads) {
-    float acc[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+  // 2. sum every rank's values in rank order (this rank's from its input), fp32, one rounding
+  uint64_t deadline = 0;
+  int timed_out = 0;
+  for (int i = threadIdx.x; i < nl; i += kArThreads) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     for (int r = 0; r < p.world; ++r) {
-      const uint4 v = __ldcg(ar_slot(own, par, r, p.max_count, e0) + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        acc[2 * k] += __uint_as_float(w[k] << 16);
-        acc[2 * k + 1] += __uint_as_float(w[k] & 0xFFFF0000u);
-      }
+      const uint2 v = (r == p.rank) ? src[i]
+                                    : ar_wait_line(ar_line(own, par, r, p.max_count, e0 / 4 + i), epoch, &deadline,
+                                                   &timed_out);
+      bf16x2_acc(a0, a1, v.x);
+      bf16x2_acc(a2, a3, v.y);
     }
-    uint4 o;
-    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
-      ow[k] = *reinterpret_cast<const uint32_t*>(&b);
-    }
-    reinterpret_cast<uint4*>(p.out + e0)[i] = o;
+    const __nv_bfloat162 b01 = __floats2bfloat162_rn(a0, a1);
+    const __nv_bfloat162 b23 = __floats2bfloat162_rn(a2, a3);
+    reinterpret_cast<uint2*>(p.out + e0)[i] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&b01), *reinterpret_cast<const uint32_t*>(&b23));
   }
-  // 5. the last CTA to finish advances the epoch for the next launch on this rank
+  if (timed_out) s_timeout = 1;
+  // 3. the last CTA to finish advances the epoch for the next launch on this rank
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (s_timeout) atomicExch(hdr, static_cast<uint32_t>(QF_ERR_TIMEOUT));
     const uint32_t done = atomicAdd(hdr + 2, 1u);
     if (done == gridDim.x - 1) {
       hdr[2] = 0u;
@@ -135,7 +114,7 @@ extern "C" {
 
 size_t qf_allreduce_buffer_bytes(int max_count) {
   if (max_count <= 0) return 0;
-  return kArData + sizeof(uint16_t) * 2 * QF_AR_MAX_RANKS * static_cast<size_t>(max_count);
+  return kArData + 4 * 2 * QF_AR_MAX_RANKS * static_cast<size_t>(max_count);  // 16-byte line per 4 elements
 }
 
 int qf_symm_alloc(size_t bytes, void** dev_ptr) {

@@ -85,15 +85,6 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
   return v;
 }
 __device__ __forceinline__ void sleep_ns(uint32_t ns) { asm volatile("nanosleep.u32 %0;" ::"r"(ns)); }
-// System-scope flag accesses for signalling between GPUs through peer (NVLink) memory.
-__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-  return v;
-}
 // Atomic add with acquire + release semantics at GPU scope: the caller's earlier writes (and those ordered before
 // it by a CTA or warp barrier) are visible to whoever observes the new value, and writes released by earlier
 // adders are visible to the caller afterwards.

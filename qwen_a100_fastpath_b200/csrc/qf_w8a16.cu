@@ -277,76 +277,56 @@ __device__ __forceinline__ MaxArg ma_shfl_xor(const MaxArg& v, int mask) {
   return MaxArg{__shfl_xor_sync(0xffffffffu, v.m, mask), __shfl_xor_sync(0xffffffffu, v.a, mask)};
 }
 
-// Fused all-reduce of one finished output tile (bf16 rows staged in sOut, [M][BN + 8]) by the epilogue warp:
-// push the tile into slot [rank] of every rank's symmetric buffer (peer stores over NVLink; the tile occupies
-// elements [tile*BN*M, (tile+1)*BN*M) of a slot, token-major), raise flag [rank][tile] on every rank
-// (system-scope release), wait (bounded) for every rank's flag [*][tile] in this rank's buffer, then sum the ranks'
-// tiles in rank order in fp32, round once to bf16 and store the rows of y.  Every rank computes the same bits.
+// Fused all-reduce of one finished output tile (bf16 rows staged in sOut, [M][BN + 8]) by the epilogue warp: write
+// the tile as self-validating lines (qf_comm.cuh) into slot [rank] of every other rank's symmetric buffer (peer
+// stores over NVLink; the tile occupies elements [tile*BN*M, (tile+1)*BN*M) of a slot, token-major), then for every
+// group of 4 outputs wait (bounded) for the other ranks' lines in this rank's buffer, sum all ranks' values in rank
+// order in fp32 (this rank's from sOut), round once to bf16 and store y.  Every rank computes the same bits.
 template <int BN>
 __device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int lane, const __nv_bfloat16* sOut,
                                                   uint32_t epoch) {
   constexpr int OS = BN + 8;
-  constexpr int TV = BN / 8;  // 16-byte vectors per token row of the tile
+  constexpr int LPR = BN / 4;  // lines per token row of the tile
   const int par = static_cast<int>(epoch & 1u);
-  const int nvec = p.M * TV;
-  const int e0 = tile * BN * p.M;
-  for (int r = 0; r < p.ar_world; ++r) {
-    uint4* dst = ar_slot(p.ar_bufs[r], par, p.ar_rank, p.ar_max_count, e0);
-    for (int idx = lane; idx < nvec; idx += 32) {
-      const int m = idx / TV;
-      dst[idx] = *reinterpret_cast<const uint4*>(sOut + m * OS + (idx - m * TV) * 8);
-    }
+  const int nl = p.M * LPR;
+  const int l0 = tile * BN * p.M / 4;
+  for (int idx = lane; idx < nl; idx += 32) {
+    const int m = idx / LPR;
+    const uint2 v = *reinterpret_cast<const uint2*>(sOut + m * OS + (idx - m * LPR) * 4);
+    const uint4 line = make_uint4(v.x, epoch, v.y, epoch);
+    for (int r = 0; r < p.ar_world; ++r)
+      if (r != p.ar_rank) st_volatile_v4(ar_line(p.ar_bufs[r], par, p.ar_rank, p.ar_max_count, l0 + idx), line);
   }
-  __syncwarp();  // every lane's stores precede the releases below
   uint8_t* own = p.ar_bufs[p.ar_rank];
-  if (lane < p.ar_world) st_release_sys(ar_flag(p.ar_bufs[lane], par, p.ar_rank, tile), epoch);
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+  uint64_t deadline = 0;
   int timed_out = 0;
-  if (lane < p.ar_world) {
-    const uint32_t* f = ar_flag(own, par, lane, tile);
-    if (ld_acquire_sys(f) != epoch) {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(f) != epoch) {
-        if (global_timer_ns() - t0 > kArWaitNs) {
-          timed_out = 1;
-          break;
-        }
-      }
+  for (int idx = lane; idx < nl; idx += 32) {
+    const int m = idx / LPR;
+    const int col = (idx - m * LPR) * 4;
+    const int n = tile * BN + col;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int r = 0; r < p.ar_world; ++r) {
+      const uint2 v = (r == p.ar_rank)
+                          ? *reinterpret_cast<const uint2*>(sOut + m * OS + col)
+                          : ar_wait_line(ar_line(own, par, r, p.ar_max_count, l0 + idx), epoch, &deadline, &timed_out);
+      bf16x2_acc(a0, a1, v.x);
+      bf16x2_acc(a2, a3, v.y);
+    }
+    __nv_bfloat16* out = y + static_cast<int64_t>(m) * p.ldy + n;
+    if (p.out_vec && n + 4 <= p.N) {
+      const __nv_bfloat162 b01 = __floats2bfloat162_rn(a0, a1);
+      const __nv_bfloat162 b23 = __floats2bfloat162_rn(a2, a3);
+      *reinterpret_cast<uint2*>(out) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&b01), *reinterpret_cast<const uint32_t*>(&b23));
+    } else {
+      const float av[4] = {a0, a1, a2, a3};
+      for (int k = 0; k < 4; ++k)
+        if (n + k < p.N) out[k] = __float2bfloat16_rn(av[k]);
     }
   }
   if (__any_sync(0xffffffffu, timed_out) && lane == 0)
     atomicExch(reinterpret_cast<uint32_t*>(own), static_cast<uint32_t>(QF_ERR_TIMEOUT));
-  __syncwarp();  // the acquiring lanes' view covers the other lanes' loads below
-  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
-  for (int idx = lane; idx < nvec; idx += 32) {
-    const int m = idx / TV;
-    const int n = tile * BN + (idx - m * TV) * 8;
-    float acc[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-    for (int r = 0; r < p.ar_world; ++r) {
-      const uint4 v = __ldcg(ar_slot(own, par, r, p.ar_max_count, e0) + idx);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        acc[2 * k] += __uint_as_float(w[k] << 16);
-        acc[2 * k + 1] += __uint_as_float(w[k] & 0xFFFF0000u);
-      }
-    }
-    __nv_bfloat16* out = y + static_cast<int64_t>(m) * p.ldy + n;
-    if (p.out_vec && n + 8 <= p.N) {
-      uint4 o;
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
-        ow[k] = *reinterpret_cast<const uint32_t*>(&b2);
-      }
-      *reinterpret_cast<uint4*>(out) = o;
-    } else {
-      for (int k = 0; k < 8; ++k)
-        if (n + k < p.N) out[k] = __float2bfloat16_rn(acc[k]);
-    }
-  }
 }
 
 // Reduction of a stream-K tile from every contributor's slot (CTAs c_first .. c_last, in that order), by the

@@ -127,4 +127,5 @@ def test_allreduce_empty_and_buffer_size():
     assert _lib.LIB.qf_allreduce_buffer_bytes(0) == 0
     small = _lib.LIB.qf_allreduce_buffer_bytes(8)
     big = _lib.LIB.qf_allreduce_buffer_bytes(16 * 5120)
-    assert big - small == (16 * 5120 - 8) * 2 * 2 * _lib.QF_AR_MAX_RANKS   # bf16 x 2 parities x 8 source slots
+    # one 16-byte line per 4 elements, 2 parities, 8 source slots
+    assert big - small == (16 * 5120 - 8) * 4 * 2 * _lib.QF_AR_MAX_RANKS
