@@ -103,6 +103,23 @@ int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t l
                           const void* bias, void* y, int64_t ldy, int y_dtype, int M, int N, int K,
                           unsigned flags, void* stream);
 
+/* gate_up projection with the MLP activation fused into its epilogue: w holds the merged [gate; up] weight (rows
+ * [0, N/2) gate, [N/2, N) up, vLLM's MergedColumnParallelLinear), and the result is the activation
+ * y[m, j] = bf16( bf16(silu(g[m, j])) * u[m, j] ), j < N/2, where g and u are the bf16 GEMM outputs of the gate and up
+ * rows -- vLLM's SiluAndMul on the gate_up output (F.silu(x[..., :I]) * x[..., I:]; the reference plugin calls the
+ * plain GEMM and leaves the activation to vLLM).  Saves the [M, N] intermediate and its separate kernel.  Arguments
+ * as qf_w8a16_gemm (bf16 output [M, N/2], no bias); N even. */
+int qf_w8a16_gemm_silu_mul(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,
+                           int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, unsigned flags, void* stream);
+
+/* Load-time int8 quantizer of the draft LM head on the device: replaces the per-row symmetric quantizer the
+ * reference runs in torch when the drafter loads (plugin/qwen_fastpath/patches.py:143-147).  w: bf16 [V, H] (row
+ * stride ldw elements); q: int8 [V, H] (row stride ldq bytes); scale: fp32 [V].  s = max(max|w|, 1e-8) / 127,
+ * q = clamp(round_half_even(w / s), -127, 127), the same fp32 operations as the reference (bit-identical).
+ * H <= 8192. */
+int qf_quantize_rows_int8(const void* w, int64_t ldw, int V, int H, int8_t* q, int64_t ldq, float* scale,
+                          void* stream);
+
 /* Reads and clears the workspace's sticky device error flag (synchronises `stream`).  *status receives
  * QF_OK or QF_ERR_TIMEOUT.  Not for the hot path. */
 int qf_workspace_status(void* ws, void* stream, int* status);

@@ -168,6 +168,18 @@ def quantize_rows(weight_bits, block_rows: int = 16384):
     return q, sc
 
 
+def silu_mul(y_bits, I: int):
+    """vLLM's SiluAndMul on the bf16 gate_up output ``y [M, 2I]`` (vllm/model_executor/layers/activation.py,
+    ``SiluAndMul.forward_native``: ``F.silu(x[..., :d]) * x[..., d:]`` on bf16 tensors): ``act = bf16(g / (1 +
+    exp(-g)))`` in fp32, ``out = bf16(act * u)``.  Returns bf16 bits ``[M, I]``."""
+    y = bf16_to_f32(y_bits)
+    g = y[:, :I].astype(np.float32)
+    u = y[:, I:2 * I].astype(np.float32)
+    with np.errstate(over="ignore"):
+        act = f32_to_bf16((g / (np.float32(1.0) + np.exp(-g))).astype(np.float32))
+    return f32_to_bf16((bf16_to_f32(act) * u).astype(np.float32))
+
+
 def top_tokens(logits_bits, num_pad: int, vocab_start: int = 0) -> np.ndarray:
     """``get_top_tokens`` (plugin/qwen_fastpath/patches.py:182-185) on bf16 logits [M, V]."""
     v = bf16_to_f32(logits_bits).astype(np.float64)

@@ -124,6 +124,7 @@ struct Params {
   int f16_path;
   uint32_t x_tx;  // activation bytes per stage: 2 B boxes of M rows x 128 bytes
   int out_vec;     // bf16 output rows (y or logits) can be written with 16-byte stores
+  int silu_I;      // > 0: gate_up with SiLU(gate) * up fused; the weight holds gate rows [0, I), up rows [I, 2I)
   // fused all-reduce of y over the tensor-parallel ranks (row-parallel layers); ar_world == 0: off
   int ar_world, ar_rank, ar_max_count;
   uint8_t* ar_bufs[QF_AR_MAX_RANKS];
@@ -197,7 +198,51 @@ __device__ __forceinline__ void store_out(const Params& p, int n, int m, float v
   }
 }
 
-// Walks a CTA's stages in order: its stream-K share of tiles 0..r-1, then its whole tiles.
+// Weight row (output channel) behind row r of tile `tile`.  With the fused SiLU gate (silu_I > 0) a tile holds BN/2
+// gate rows in its first half and the matching up rows in its second half.  Returns -1 for rows past the end.
+template <int BN, bool SILU>
+__device__ __forceinline__ int weight_row(const Params& p, int tile, int r) {
+  if constexpr (!SILU) {
+    const int n = tile * BN + r;
+    return n < p.N ? n : -1;
+  }
+  constexpr int H = BN / 2;
+  const int j = tile * H + (r < H ? r : r - H);
+  if (j >= p.silu_I) return -1;
+  return r < H ? j : p.silu_I + j;
+}
+
+// Fused gate_up activation for a finished tile staged in sOut ([M][BN + 8] bf16: gate in columns [0, BN/2), up in
+// [BN/2, BN)): y[m, j] = bf16( bf16(silu(g)) * u ), silu(g) = g / (1 + exp(-g)) in fp32 -- the two roundings of
+// vLLM's SiluAndMul on bf16 tensors (F.silu(x[..., :I]) * x[..., I:]).  16-byte stores of 8 outputs.
+template <int BN>
+__device__ __forceinline__ void silu_mul_store(const Params& p, int tile, int lane, const __nv_bfloat16* sOut) {
+  constexpr int OS = BN + 8;
+  constexpr int H = BN / 2;
+  constexpr int HC = H / 8;
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+  for (int idx = lane; idx < p.M * HC; idx += 32) {
+    const int m = idx / HC;
+    const int c = (idx - m * HC) * 8;
+    const int j = tile * H + c;
+    const __nv_bfloat16* gp = sOut + m * OS + c;
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float gv = __bfloat162float(gp[e]);
+      const __nv_bfloat16 act = __float2bfloat16_rn(gv / (1.0f + expf(-gv)));
+      o[e] = __float2bfloat16_rn(__bfloat162float(act) * __bfloat162float(gp[H + e]));
+    }
+    __nv_bfloat16* out = y + static_cast<int64_t>(m) * p.ldy + j;
+    if (p.out_vec && j + 8 <= p.silu_I) {
+      *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(o);
+    } else {
+      for (int e = 0; e < 8; ++e)
+        if (j + e < p.silu_I) out[e] = o[e];
+    }
+  }
+}
+
 // Walks a CTA's stages in order: its stream-K share of tiles 0..r-1, then its whole tiles.
 struct StageIter {
   int tile, kk, i;
@@ -332,7 +377,7 @@ __device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int
 // Reduction of a stream-K tile from every contributor's slot (CTAs c_first .. c_last, in that order), by the
 // contributor that arrived last when the tile's designated reducer did not wait for the others: finishes the tile
 // (scale + store, or logits + tile statistics for the head) and re-arms the tile's counter.
-template <int BN, int NT, bool HEAD, bool AR>
+template <int BN, int NT, bool HEAD, bool AR, bool SILU>
 __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int lane, int c_first, int c_last,
                                                  int* counters, const float* partials, float4* sTile,
                                                  __nv_bfloat16* sOut, uint32_t ar_epoch) {
@@ -377,15 +422,17 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
     }
 #pragma unroll
     for (int j = 0; j < PC; ++j) {
-      const int n = tile * BN + (lane + 32 * (pass * PC + j)) / (2 * NT);
-      const float sc = n < p.N ? __ldg(p.scale + n) : 0.f;
+      const int row = (lane + 32 * (pass * PC + j)) / (2 * NT);
+      const int wr = weight_row<BN, SILU>(p, tile, row);
+      const int n = wr < 0 ? p.N : wr;  // past the end: masked below
+      const float sc = wr >= 0 ? __ldg(p.scale + wr) : 0.f;
       const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int m = m_base + e;
         if constexpr (!HEAD) {
-          if constexpr (AR)  // staged like finish_tile, published below
-            sOut[m * (BN + 8) + (lane + 32 * (pass * PC + j)) / (2 * NT)] = __float2bfloat16_rn(vv[e] * sc);
+          if constexpr (AR || SILU)  // staged like finish_tile, published / activated below
+            sOut[m * (BN + 8) + row] = __float2bfloat16_rn(vv[e] * sc);
           else
             store_out(p, n, m, vv[e] * sc);
         } else {
@@ -411,6 +458,10 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
   if constexpr (AR) {
     __syncwarp();
     ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch);
+  } else if constexpr (SILU) {
+    __syncwarp();
+    silu_mul_store<BN>(p, tile, lane, sOut);
+    __syncwarp();
   }
   if (lane == 0) counters[tile] = 0;  // ready for the next call on this workspace
 }
@@ -419,7 +470,7 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
 // tokens 8 nt + 2 t and 8 nt + 2 t + 1): scale, bf16 rounding (+ the bias as a second rounding), rows staged in
 // shared memory and written with 16-byte stores (GEMM output or head logits), and for the head the tile's per-token
 // (max, first argmax, sum exp) of its bf16 logits.
-template <int BN, int NT, bool HEAD, bool AR>
+template <int BN, int NT, bool HEAD, bool AR, bool SILU>
 __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane, const float (&v)[BN / 16][NT][4],
                                             const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* sTile,
                                             uint32_t ar_epoch) {
@@ -485,6 +536,8 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
   const int64_t ld = HEAD ? p.ldl : p.ldy;
   if constexpr (AR) {
     ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch);
+  } else if constexpr (SILU) {
+    silu_mul_store<BN>(p, tile, lane, sOut);
   } else if (dst) {
     constexpr int CH = BN / 8;
     for (int idx = lane; idx < p.M * CH; idx += 32) {
@@ -560,11 +613,12 @@ __device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTi
   __syncwarp();
 }
 
-template <int BN, int NT, int KS, bool HEAD, bool AR>
+template <int BN, int NT, int KS, bool HEAD, bool AR, bool SILU>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  const Params p) {
   static_assert(!(HEAD && AR), "the head is vocab-parallel: no all-reduce");
+  static_assert(!(SILU && (HEAD || AR)), "the fused gate is for the column-parallel gate_up only");
   using C = Geo<BN, NT, KS>;
   constexpr int S = C::kStages;
   constexpr int B = C::B;
@@ -627,9 +681,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < npre; ++i) {  // weights do not depend on the previous kernel
         mbar_arrive_expect_tx(&full_bar[i], C::kWBytes + p.x_tx);
 #pragma unroll
-        for (int b = 0; b < B; ++b)
-          tma_load_2d(sW + i * C::kWBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[i], pi.kk * KS + b * 128,
-                      pi.tile * BN, pol_w);
+        for (int b = 0; b < B; ++b) {
+          uint8_t* dst = sW + i * C::kWBytes + b * C::kWBoxBytes;
+          if constexpr (!SILU) {
+            tma_load_2d(dst, &tmap_w, &full_bar[i], pi.kk * KS + b * 128, pi.tile * BN, pol_w);
+          } else {  // half-height boxes: gate rows, then the matching up rows
+            tma_load_2d(dst, &tmap_w, &full_bar[i], pi.kk * KS + b * 128, pi.tile * (BN / 2), pol_w);
+            tma_load_2d(dst + (BN / 2) * 128, &tmap_w, &full_bar[i], pi.kk * KS + b * 128,
+                        p.silu_I + pi.tile * (BN / 2), pol_w);
+          }
+        }
         pi.next(p);
       }
       pdl_wait();
@@ -652,9 +713,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive_expect_tx(&full_bar[s], C::kWBytes + p.x_tx);
 #pragma unroll
-        for (int b = 0; b < B; ++b)
-          tma_load_2d(sW + s * C::kWBytes + b * C::kWBoxBytes, &tmap_w, &full_bar[s], pi.kk * KS + b * 128,
-                      pi.tile * BN, pol_w);
+        for (int b = 0; b < B; ++b) {
+          uint8_t* dst = sW + s * C::kWBytes + b * C::kWBoxBytes;
+          if constexpr (!SILU) {
+            tma_load_2d(dst, &tmap_w, &full_bar[s], pi.kk * KS + b * 128, pi.tile * BN, pol_w);
+          } else {  // half-height boxes: gate rows, then the matching up rows
+            tma_load_2d(dst, &tmap_w, &full_bar[s], pi.kk * KS + b * 128, pi.tile * (BN / 2), pol_w);
+            tma_load_2d(dst + (BN / 2) * 128, &tmap_w, &full_bar[s], pi.kk * KS + b * 128,
+                        p.silu_I + pi.tile * (BN / 2), pol_w);
+          }
+        }
         uint8_t* xs = sX + s * C::kXStageBytes;
 #pragma unroll
         for (int b = 0; b < 2 * B; ++b)
@@ -727,9 +795,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float sc[MT][2];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        const int n0 = tile * BN + 16 * mt + g;
-        sc[mt][0] = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
-        sc[mt][1] = n0 + 8 < p.N ? __ldg(p.scale + n0 + 8) : 0.f;
+        const int w0 = weight_row<BN, SILU>(p, tile, 16 * mt + g);
+        const int w1 = weight_row<BN, SILU>(p, tile, 16 * mt + g + 8);
+        sc[mt][0] = w0 >= 0 ? __ldg(p.scale + w0) : 0.f;
+        sc[mt][1] = w1 >= 0 ? __ldg(p.scale + w1) : 0.f;
       }
       int c_first = 0, c_last = 0;
       if (is_red || is_con) {
@@ -822,12 +891,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                  static_cast<uint32_t>(c_last - c_first);
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          split_reduce_all<BN, NT, HEAD, AR>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut, ar_epoch);
+          split_reduce_all<BN, NT, HEAD, AR, SILU>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut, ar_epoch);
           if constexpr (HEAD) fold_tile(p, lane, sStat, run);
         }
         continue;
       }
-      finish_tile<BN, NT, HEAD, AR>(p, tile, lane, v, sc, sOut, sStat, ar_epoch);
+      finish_tile<BN, NT, HEAD, AR, SILU>(p, tile, lane, v, sc, sOut, sStat, ar_epoch);
       if constexpr (HEAD) fold_tile(p, lane, sStat, run);
     }
     if (AR && lane == 0) {  // the last CTA to finish advances the buffers' epoch for the next call
@@ -1089,11 +1158,11 @@ void pick_tiles(int N, int K, int sms, int* bn, int* ks) {
   }
 }
 
-template <int BN, int NT, int KS, bool HEAD, bool AR>
+template <int BN, int NT, int KS, bool HEAD, bool AR, bool SILU>
 int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
            unsigned flags, cudaStream_t stream) {
   using C = Geo<BN, NT, KS>;
-  auto kern = w8a16_kernel<BN, NT, KS, HEAD, AR>;
+  auto kern = w8a16_kernel<BN, NT, KS, HEAD, AR, SILU>;
   static bool smem_attr_set[64] = {};
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -1105,7 +1174,7 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   }
   CUtensorMap tw, tx;
   int rc = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
-                     static_cast<uint64_t>(ldw), 128, BN);
+                     static_cast<uint64_t>(ldw), 128, p.silu_I ? BN / 2 : BN);
   if (rc) return rc;
   // activation boxes are M rows high: only the real tokens are copied
   const uint64_t xstride = (p.M > 1) ? static_cast<uint64_t>(ldx) * 2 : (static_cast<uint64_t>(p.K) * 2 + 15) / 16 * 16;
@@ -1116,7 +1185,7 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   p.f16_path = f16_path();
   p.x_tx = static_cast<uint32_t>(2 * C::B * p.M * 128);
   p.kiters = (p.K + KS - 1) / KS;
-  p.ntiles = (p.N + BN - 1) / BN;
+  p.ntiles = p.silu_I ? (p.silu_I + BN / 2 - 1) / (BN / 2) : (p.N + BN - 1) / BN;
   if (p.ntiles > kMaxTiles) return fail(QF_ERR_SHAPE, "too many tiles for this tile height");
   if (p.ar_world && (p.ntiles > QF_AR_MAX_CHUNKS || static_cast<long long>(p.ntiles) * BN * p.M > p.ar_max_count))
     return fail(QF_ERR_SHAPE, "output too large for the all-reduce buffers (max_count) or more than "
@@ -1152,11 +1221,11 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   return QF_OK;
 }
 
-template <int BN, int KS, bool HEAD, bool AR>
+template <int BN, int KS, bool HEAD, bool AR, bool SILU>
 int launch_nt(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
               unsigned flags, cudaStream_t st) {
-  if (p.M <= 8) return launch<BN, 1, KS, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  return launch<BN, 2, KS, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (p.M <= 8) return launch<BN, 1, KS, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  return launch<BN, 2, KS, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
 // Optional fixed tile shape (environment QF_TILES="BN:KS", read once; 0 = the per-shape choice): used by the
@@ -1175,17 +1244,17 @@ const TileShape& tile_override() {
   return v;
 }
 
-template <bool HEAD, bool AR = false>
+template <bool HEAD, bool AR = false, bool SILU = false>
 int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
                unsigned flags, cudaStream_t st) {
   int bn = tile_override().bn, ks = tile_override().ks;
   if (bn == 0) pick_tiles(p.N, p.K, dinfo->sm_count, &bn, &ks);
-  if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 64 && ks == 512) return launch_nt<64, 512, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 32 && ks == 512) return launch_nt<32, 512, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 32 && ks == 1024) return launch_nt<32, 1024, HEAD, AR>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 512) return launch_nt<64, 512, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 512) return launch_nt<32, 512, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 1024) return launch_nt<32, 1024, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
   return fail(QF_ERR_SHAPE, "no kernel instance for the chosen tile shape");
 }
 
@@ -1255,6 +1324,32 @@ int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
   return launch_any<false>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+}
+
+int qf_w8a16_gemm_silu_mul(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,
+                           int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, unsigned flags, void* stream) {
+  int rc = check_common(x, ldx, w, ldw, scale, M, N, K, ws, ws_bytes);
+  if (rc) return rc;
+  if (N % 2) return fail(QF_ERR_SHAPE, "N must be even (gate rows [0, N/2), up rows [N/2, N))");
+  if (M == 0 || N == 0) return QF_OK;
+  if (K == 0) return fail(QF_ERR_SHAPE, "the fused gate needs K >= 1");
+  if (!y) return fail(QF_ERR_INVALID, "null y");
+  if (M > 1 && ldy < N / 2) return fail(QF_ERR_STRIDE, "ldy < N / 2");
+  int dev;
+  DeviceInfo* dinfo;
+  rc = device_info(&dev, &dinfo);
+  if (rc) return rc;
+  Params p = {};
+  p.scale = scale;
+  p.y = y;
+  p.ldy = ldy;
+  p.out_vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (M == 1 || ldy % 8 == 0);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ws = static_cast<uint8_t*>(ws);
+  p.silu_I = N / 2;
+  return launch_any<false, false, true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
 }
 
 int qf_w8a16_gemm_allreduce(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,

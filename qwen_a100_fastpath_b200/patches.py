@@ -89,11 +89,19 @@ def patch_int8_linear() -> bool:
 # ----------------------------------------------------------------------------------------------
 def quantize_head_rows(weight: torch.Tensor, block_rows: int = 16384):
     """Per-row symmetric int8 copy of an lm_head weight ``[V, H]`` (patches.py:143-147): ``s = max|w| / 127``
-    (at least 1e-8 / 127), ``q = clamp(round_half_even(w / s), -127, 127)``, processed in 16384-row blocks so
-    the fp32 temporaries stay small.  Returns (int8 ``[V, H]``, fp32 ``[V]``) on the weight's device."""
+    (at least 1e-8 / 127), ``q = clamp(round_half_even(w / s), -127, 127)``.  Returns (int8 ``[V, H]``, fp32
+    ``[V]``) on the weight's device.  A bf16 CUDA weight is quantized by the library's device kernel
+    (``qf_quantize_rows_int8``, one pass, bit-identical); a weight still on the host (loading) goes through the
+    reference's torch arithmetic in 16384-row blocks so the fp32 temporaries stay small."""
     V, H = weight.shape
     w8 = torch.empty((V, H), dtype=torch.int8, device=weight.device)
     scale = torch.empty((V,), dtype=torch.float32, device=weight.device)
+    if weight.is_cuda and weight.dtype == torch.bfloat16 and weight.stride(1) == 1 and H <= 8192:
+        from ._lib import LIB, check
+        check("qf_quantize_rows_int8", LIB.qf_quantize_rows_int8(
+            weight.data_ptr(), weight.stride(0), V, H, w8.data_ptr(), H, scale.data_ptr(),
+            torch.cuda.current_stream(weight.device).cuda_stream))
+        return w8, scale
     with torch.no_grad():
         for r0 in range(0, V, block_rows):
             rows = weight[r0:r0 + block_rows].float()

@@ -156,6 +156,38 @@ def w8a16_mm(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, cfg=None
     return out
 
 
+def w8a16_mm_silu_mul(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, out: torch.Tensor | None = None,
+                      pdl: bool | None = None) -> torch.Tensor:
+    """gate_up projection with vLLM's SiluAndMul fused (``qf_w8a16_gemm_silu_mul``): ``w_t [K, 2I]`` holds the merged
+    gate (columns ``[0, I)``) and up (``[I, 2I)``) weights, ``w_scale [2I]``; returns ``[M, I]`` bf16
+    ``bf16(bf16(silu(g)) * u)`` with ``g``, ``u`` the bf16 GEMM outputs -- the same as ``F.silu(y[:, :I]) * y[:, I:]``
+    on ``y = w8a16_mm(x, w_t, w_scale)``."""
+    if x.dim() != 2 or w_t.shape[0] != x.shape[1]:
+        raise ValueError("x must be [M, K] matching w_t [K, N]")
+    M, K = x.shape
+    N = w_t.shape[1]
+    if N % 2 or M > SMALL_M or K < 1:
+        raise ValueError(f"need an even N, K >= 1 and M <= {SMALL_M}")
+    if not (x.is_cuda and w_t.is_cuda and w_scale.is_cuda) or x.dtype != torch.bfloat16:
+        raise ValueError("libqf_b200 needs CUDA tensors and bf16 activations (there is no CPU path)")
+    scale = w_scale.reshape(-1).contiguous()
+    if scale.numel() != N or scale.dtype != torch.float32:
+        raise ValueError("w_scale must hold N fp32 per-channel scales")
+    ldw = _check_weight(w_t, K)
+    x = _aligned_rows(x)
+    if out is None:
+        out = torch.empty((M, N // 2), dtype=torch.bfloat16, device=x.device)
+    elif out.shape != (M, N // 2) or out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError("out must be bf16 [M, N/2] with unit column stride")
+    stream = torch.cuda.current_stream(x.device)
+    ws = workspace(x.device, stream, LIB.qf_w8a16_workspace_bytes(M, N, K))
+    flags = _lib.QF_FLAG_PDL if (_PDL_DEFAULT if pdl is None else pdl) else 0
+    rc = LIB.qf_w8a16_gemm_silu_mul(x.data_ptr(), x.stride(0), w_t.data_ptr(), ldw, scale.data_ptr(), out.data_ptr(),
+                                    out.stride(0), M, N, K, ws.data_ptr(), ws.numel(), flags, stream.cuda_stream)
+    check("qf_w8a16_gemm_silu_mul", rc)
+    return out
+
+
 def w8a16_mm_allreduce(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, comm, out: torch.Tensor | None = None,
                        pdl: bool | None = None) -> torch.Tensor:
     """Row-parallel layer with its all-reduce fused into the GEMM (``qf_w8a16_gemm_allreduce``): this rank holds the

@@ -13,7 +13,7 @@ def main() -> int:
     from oracle import w8a16_oracle as orc
     from qwen_a100_fastpath_b200.w8a16 import pick_config, w8a16_head, w8a16_mm
     from tests.conftest import from_dev_bf16, to_dev_bf16
-    from tests.test_gpu_gemm import bf16_close
+    from tests.test_gpu_gemm import bf16_close, silu_close
     dev = torch.device("cuda", 0)
     for (N, K, M) in [(1000, 1024, 5), (10240, 1024, 3), (4100, 2048, 12), (19072, 512, 1)]:
         x, W, s = orc.make_inputs(N + K + M, M, N, K)
@@ -21,6 +21,13 @@ def main() -> int:
                      pick_config(N, K), torch.bfloat16)
         torch.cuda.synchronize()
         bf16_close(from_dev_bf16(y), orc.w8a16_mm(x, W, s, "bf16"))
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_mm_silu_mul
+    for (I, K, M) in [(1000, 1024, 5), (4100, 2048, 12)]:  # fused gate_up activation on the same schedules
+        x, W, s = orc.make_inputs(I + K, M, 2 * I, K)
+        out = w8a16_mm_silu_mul(to_dev_bf16(x, dev), torch.from_numpy(W).to(dev).t(), torch.from_numpy(s).to(dev))
+        torch.cuda.synchronize()
+        y_orc = orc.w8a16_mm(x, W, s, "bf16")
+        silu_close(from_dev_bf16(out), orc.silu_mul(y_orc, I), y_orc, I)
     for (V, H, M, pad) in [(4100, 2048, 4, 36), (16384 + 640, 1024, 16, 64)]:
         x, W, s = orc.make_inputs(V + H, M, V, H)
         logits, mx, am, lse = w8a16_head(to_dev_bf16(x, dev), torch.from_numpy(W).to(dev).t(),

@@ -233,3 +233,43 @@ def test_nan_activation_propagates(dev):
     *_, y = run_case(dev, M, N, K, seed=0, x_bits=x, W=W, s=s)
     yf = y.float().cpu().numpy()
     assert np.isnan(yf[1]).all() and np.isfinite(yf[[0, 2]]).all()
+
+
+@pytest.mark.parametrize("I,K,M", [(17408, 5120, 5), (17408, 5120, 16), (1000, 1024, 3), (4352, 5120, 1),
+                                   (8704, 2048, 12)])
+def test_fused_silu_mul_gate_up(dev, I, K, M):
+    """qf_w8a16_gemm_silu_mul == vLLM's SiluAndMul (oracle.silu_mul) on the gate_up GEMM output: against the oracle's
+    own GEMM, and against torch's F.silu(y[:, :I]) * y[:, I:] on this library's plain GEMM output (the fused kernel
+    splits tiles differently, so a few outputs may differ by the bf16 ulp their inputs differ by)."""
+    import torch
+    import torch.nn.functional as F
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_mm, w8a16_mm_silu_mul
+    x_bits, W, s = orc.make_inputs(3 * I + K + M, M, 2 * I, K)
+    x = to_dev_bf16(x_bits, dev)
+    wt = torch.from_numpy(W).to(dev).t()
+    st = torch.from_numpy(s).to(dev)
+    out = w8a16_mm_silu_mul(x, wt, st)
+    y = w8a16_mm(x, wt, st, None, torch.bfloat16)
+    ref_gpu = F.silu(y[:, :I]) * y[:, I:]
+    torch.cuda.synchronize()
+    silu_close(from_dev_bf16(out), from_dev_bf16(ref_gpu), from_dev_bf16(y), I)
+    y_orc = orc.w8a16_mm(x_bits, W, s, "bf16")
+    silu_close(from_dev_bf16(out), orc.silu_mul(y_orc, I), y_orc, I)
+
+
+def silu_close(out_bits, ref_bits, y_bits, I, max_mismatch_frac=0.02):
+    """The fused activation against a reference built from gate/up values ``y`` that may each differ from the
+    kernel's by one bf16 ulp (fp32 summation order): the tolerance propagates those ulps through
+    ``silu(g) * u`` (|d/du| = |silu(g)|, |d/dg| <= 1.1 |u|) plus one ulp of the output and 2^-16 max|ref|."""
+    def ulp(v):
+        return np.spacing(np.abs(v).astype(np.float32)).astype(np.float64) * 2.0 ** 16
+    out = orc.bf16_to_f32(out_bits).astype(np.float64)
+    ref = orc.bf16_to_f32(ref_bits).astype(np.float64)
+    y = orc.bf16_to_f32(y_bits).astype(np.float64)
+    g, u = y[:, :I], y[:, I:2 * I]
+    silu = g / (1.0 + np.exp(-np.clip(g, -80, 80)))
+    tol = ulp(np.maximum(np.abs(out), np.abs(ref))) + np.abs(silu) * ulp(u) + 1.1 * np.abs(u) * ulp(g) + \
+        2.0 ** -16 * np.abs(ref).max()
+    bad = np.abs(out - ref) > tol
+    assert not bad.any(), f"{int(bad.sum())} outputs beyond the propagated tolerance"
+    assert np.mean(np.asarray(out_bits) != np.asarray(ref_bits)) <= max_mismatch_frac

@@ -102,3 +102,28 @@ def test_head_deterministic(dev):
     for u, v in zip(a, b):
         assert torch.equal(u.view(torch.uint8) if u.dtype != torch.bfloat16 else u.view(torch.int16),
                            v.view(torch.uint8) if v.dtype != torch.bfloat16 else v.view(torch.int16))
+
+
+def test_device_quantizer_bit_exact(dev):
+    """qf_quantize_rows_int8 (via patches.quantize_head_rows on a CUDA weight) == the reference quantizer
+    (patches.py:143-147, oracle.quantize_rows), bit for bit: the golden head weight (zero row, large outlier) and a
+    random Qwen-width block."""
+    import json
+    from pathlib import Path
+
+    import torch
+
+    from qwen_a100_fastpath_b200.patches import quantize_head_rows
+    meta = json.loads((Path(__file__).resolve().parent / "golden" / "reference_outputs.json").read_text())["head"]
+    rs = np.random.RandomState(meta["weight_seed"])
+    wf = rs.standard_normal((meta["V"], meta["H"])).astype(np.float32) * 0.05
+    wf[7] = 0.0
+    wf[11, 3] = 40.0
+    cases = [orc.f32_to_bf16(wf),
+             orc.f32_to_bf16(np.random.RandomState(5).standard_normal((3000, 5120)).astype(np.float32) * 0.02)]
+    for wb in cases:
+        q, s = quantize_head_rows(to_dev_bf16(wb, dev))
+        torch.cuda.synchronize()
+        q_ref, s_ref = orc.quantize_rows(wb)
+        assert np.array_equal(q.cpu().numpy(), q_ref)
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))

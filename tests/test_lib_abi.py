@@ -129,3 +129,14 @@ def test_allreduce_empty_and_buffer_size():
     big = _lib.LIB.qf_allreduce_buffer_bytes(16 * 5120)
     # one 16-byte line per 4 elements, 2 parities, 8 source slots
     assert big - small == (16 * 5120 - 8) * 4 * 2 * _lib.QF_AR_MAX_RANKS
+
+
+@pytest.mark.parametrize("args,code", [
+    ((FAKE, 5120, -1, 5120, FAKE, 5120, FAKE, None), -2),
+    ((FAKE, 9000, 4, 9000, FAKE, 9000, FAKE, None), -2),      # rows wider than 8192
+    ((None, 5120, 4, 5120, FAKE, 5120, FAKE, None), -1),
+    ((FAKE, 100, 4, 5120, FAKE, 5120, FAKE, None), -3),      # ldw < H
+])
+def test_quantizer_argument_validation(args, code):
+    assert _lib.LIB.qf_quantize_rows_int8(*args) == code
+    assert _lib.LIB.qf_quantize_rows_int8(FAKE, 64, 0, 64, FAKE, 64, FAKE, None) == 0   # V == 0: no-op

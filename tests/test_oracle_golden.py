@@ -146,3 +146,16 @@ def test_row_parallel_partials_sum_to_full():
     for world in (2, 4, 8):
         acc = sum(orc.dequant_matmul_f64(*reversed(orc.shard_rows(W, x, r, world)), s) for r in range(world))
         np.testing.assert_allclose(acc, full, rtol=1e-12, atol=1e-9)
+
+
+def test_silu_mul_oracle_matches_torch_on_bf16():
+    """oracle.silu_mul reproduces torch's F.silu(g) * u on bf16 tensors (vLLM SiluAndMul.forward_native) on CPU."""
+    import torch
+    import torch.nn.functional as F
+    rs = np.random.RandomState(3)
+    y = orc.f32_to_bf16(rs.standard_normal((4, 2 * 300)).astype(np.float32) * 3)
+    yt = torch.from_numpy(y.view(np.int16)).view(torch.bfloat16)
+    ref = (F.silu(yt[:, :300]) * yt[:, 300:]).view(torch.int16).numpy().view(np.uint16)
+    got = orc.silu_mul(y, 300)
+    assert np.mean(got != ref) < 0.01          # exp implementations may differ by an ulp before the bf16 rounding
+    assert np.all(np.abs(orc.bf16_to_f32(got) - orc.bf16_to_f32(ref)) <= np.spacing(np.abs(orc.bf16_to_f32(ref)).astype(np.float32)) * 2 ** 16 + 1e-30)
