@@ -8,9 +8,9 @@
 //
 // The contraction streams N*K int8 weight bytes once and is bound by HBM bandwidth at these M.  Design:
 //
-// * Tiles of BN output channels (BN = 128, 64 or 32, picked per shape so that there are at least as many tiles
-//   as SMs) and pipeline stages of BN x KS weight bytes (KS = 16384 / BN: a stage is always 16 KiB, i.e. 128,
-//   256 or 512 contiguous bytes of each weight row).  One persistent CTA per SM.
+// * Tiles of BN output channels (BN = 128, 64 or 32, picked per shape) and pipeline stages of BN x KS weight
+//   bytes (the per-shape choice uses KS = 32768 / BN: 32 KiB stages of 256, 512 or 1024 contiguous bytes of each
+//   weight row; 16 KiB stages exist for tuning).  One persistent CTA per SM.
 // * Data-parallel + stream-K schedule: with ntiles = q*G + r, every CTA owns q whole tiles ("DP") and an equal
 //   share of the r * kiters stages of the remaining r tiles ("SK").  Each CTA runs its SK share first: the SK
 //   tiles' partial sums are handed to a fixup warp that reduces them (fp32 partials in the workspace, summed in
@@ -21,9 +21,9 @@
 //   [8*NT tokens x 64 bf16] (cp.async.bulk.tensor, 128-byte swizzle, no multicast) into a ring of up to 10
 //   stages guarded by mbarriers.  With programmatic dependent launch the weight boxes of the first stages are
 //   issued before griddepcontrol.wait, while the previous kernel on the stream still runs.
-// * Eight consumer warps.  Warp (u, h): unit u = (weight box b, pair of m-tiles mp), h = half of each box's
-//   16-byte k chunks; lane (g, t) takes chunk c = (t ^ h) | ((t & 1) << 2), which keeps both the swizzled weight
-//   reads and the activation reads free of bank conflicts.  Weights are converted to exact 16-bit floats in
+// * Eight consumer warps.  Warp (u, h): unit u = (weight box b, group of MW = 2 or 4 m-tiles), h = half of each
+//   box's 16-byte k chunks; lane (g, t) takes chunk c = (t ^ h) | ((t & 1) << 2), which keeps both the swizzled
+//   weight reads and the activation reads free of bank conflicts.  Weights are converted to exact 16-bit floats in
 //   registers and fed to mma.sync m16n8k16 as the 16-row A operand ("swap AB"); the M <= 16 tokens are the
 //   8-column B operand (NT = 1 or 2 token tiles).  fp16 path: each warp converts its activation fragments
 //   bf16 -> fp16 (pairs (k, k+2), (k+1, k+3)) and the weights with one lop3 per byte pair; if any activation
@@ -81,14 +81,17 @@ constexpr size_t kWsBytes = kWsCtaStats + sizeof(float4) * 16 * kMaxGrid;  // fl
 template <int BN, int NT, int KS> struct Geo {
   static constexpr int B = KS / 128;                            // 128-byte weight boxes per stage
   static constexpr int MT = BN / 16;                            // m-tiles per tile (8, 4, 2)
-  static constexpr int NMP = MT / 2;                            // m-tile pairs (one per consumer warp pair)
-  static constexpr int BPW = B * NMP / 4;                       // weight boxes per consumer warp per stage
+  // m-tiles per consumer warp: 4 where the stage's boxes still split evenly over the four warp pairs, else 2.
+  // A warp converts its activation fragments once per box and reuses them for all MW of its m-tiles.
+  static constexpr int MW = (MT >= 4 && (B * (MT / 4)) % 4 == 0) ? 4 : 2;
+  static constexpr int NMW = MT / MW;                           // m-tile groups (one per consumer warp pair)
+  static constexpr int BPW = B * NMW / 4;                       // weight boxes per consumer warp per stage
   static constexpr int kWBoxBytes = BN * 128;
   static constexpr int kWBytes = BN * KS;                       // weight bytes per stage
   static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT tokens][64 bf16] (rows >= M stay zero)
   static constexpr int kXStageBytes = 2 * B * kXBoxBytes;
   static constexpr int kStageBytes = kWBytes + kXStageBytes;
-  static constexpr int kRedBytes = kConsumerWarps * 2 * 32 * 4 * NT * 4;  // [warp][m-tile of pair][lane][4NT]
+  static constexpr int kRedBytes = kConsumerWarps * MW * 32 * 4 * NT * 4;  // [warp][m-tile of group][lane][4NT]
   static constexpr int kStatBytes = 8 * 16 * 16;                          // float4 [m-tile][token]
   static constexpr int kOutStride = BN + 8;                               // bf16 [16 tokens][BN + 8] (padded)
   static constexpr int kOutBytes = 16 * kOutStride * 2;
@@ -103,7 +106,7 @@ template <int BN, int NT, int KS> struct Geo {
   static constexpr int kOffBar = kOffOut + kOutBytes;         // full[S], empty[S]
   static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;  // abort, last
   static constexpr int kSmemBytes = kOffFlag + 64 + 1024;     // + alignment slack
-  static_assert(BPW >= 1 && B * NMP == 4 * BPW, "the four warp pairs cover the stage's boxes evenly");
+  static_assert(BPW >= 1 && B * NMW == 4 * BPW && 4 % NMW == 0, "the four warp pairs cover the stage's boxes evenly");
   static_assert(kStages >= 3, "pipeline too shallow");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
@@ -623,7 +626,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = C::kStages;
   constexpr int B = C::B;
   constexpr int MT = C::MT;
-  constexpr int NMP = C::NMP;
+  constexpr int MW = C::MW;
+  constexpr int NMW = C::NMW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -855,11 +859,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
-        for (int bb = 0; bb < 4 / NMP; ++bb)  // warps (u = bb * NMP + mt / 2, h) hold m-tile mt
+        for (int bb = 0; bb < 4 / NMW; ++bb)  // warps (u = bb * NMW + mt / MW, h) hold m-tile mt
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const int src = 2 * (bb * NMP + (mt >> 1)) + hh;
-            const float* o = sRed + ((src * 2 + (mt & 1)) * 32 + lane) * 4 * NT;
+            const int src = 2 * (bb * NMW + mt / MW) + hh;
+            const float* o = sRed + ((src * MW + mt % MW) * 32 + lane) * 4 * NT;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -915,17 +919,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // -------------------------------------------------------------------- consumers (8 warps)
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
-  // Warp (u, h), u = warp / 2: m-tile pair mp = u % NMP, weight boxes b = u / NMP + j * (4 / NMP), j < BPW.
+  // Warp (u, h), u = warp / 2: m-tile group mg = u % NMW (m-tiles MW * mg ..), weight boxes
+  // b = u / NMW + j * (4 / NMW), j < BPW.
   const int h = warp & 1;           // which half of each box's 16-byte k chunks
   const int u = warp >> 1;
-  const int mp = u % NMP;
-  const int b0 = u / NMP;
+  const int mg = u % NMW;
+  const int b0 = u / NMW;
   const int g = lane >> 2;
   const int t = lane & 3;
   const int c = (t ^ h) | ((t & 1) << 2);  // this lane's 16-k chunk of the box
   const uint32_t sW_u32 = smem_u32(sW);
   const uint32_t sX_u32 = smem_u32(sX);
-  const uint32_t w_off = static_cast<uint32_t>(b0 * C::kWBoxBytes + (32 * mp + g) * 128 + ((c ^ g) << 4));
+  const uint32_t w_off = static_cast<uint32_t>(b0 * C::kWBoxBytes + (16 * MW * mg + g) * 128 + ((c ^ g) << 4));
   const uint32_t x_off = static_cast<uint32_t>((2 * b0 + (c >> 2)) * C::kXBoxBytes + g * 128);
   const uint32_t x_u0 = static_cast<uint32_t>(((2 * (c & 3)) ^ g) << 4);
   const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
@@ -933,9 +938,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool use_f16 = p.f16_path != 0;
   int tcount = 0;
 
-  float acc[2][NT][4];
+  float acc[MW][NT][4];
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
+  for (int j = 0; j < MW; ++j)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -949,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 #pragma unroll
     for (int jb = 0; jb < C::BPW; ++jb) {
-      const int db = jb * (4 / NMP);  // box offset from b0
+      const int db = jb * (4 / NMW);  // box offset from b0
       const uint32_t xbase = sX_u32 + s * C::kXStageBytes + x_off + 2 * db * C::kXBoxBytes;
       uint4 xa[NT], xb[NT];
 #pragma unroll
@@ -958,8 +963,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         xb[nt] = lds128(xbase + nt * 1024 + x_u1);
       }
       const uint32_t wbase = sW_u32 + s * C::kWBytes + w_off + db * C::kWBoxBytes;
-      const uint4 ra0 = lds128(wbase), rb0 = lds128(wbase + 1024);
-      const uint4 ra1 = lds128(wbase + 2048), rb1 = lds128(wbase + 3072);
+      uint4 ra[MW], rb[MW];  // m-tile j: rows g and g + 8 of the tile's 16
+#pragma unroll
+      for (int j = 0; j < MW; ++j) {
+        ra[j] = lds128(wbase + j * 2048);
+        rb[j] = lds128(wbase + j * 2048 + 1024);
+      }
       if (jb == C::BPW - 1) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[s]);  // release: this warp's reads of the slot are done
@@ -979,11 +988,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         f16 = !__any_sync(0xffffffffu, bad != 0);
       }
       if (f16) {
-        mma_chunk<NT, true>(acc[0], ra0, rb0, xa16, xb16);
-        mma_chunk<NT, true>(acc[1], ra1, rb1, xa16, xb16);
+#pragma unroll
+        for (int j = 0; j < MW; ++j) mma_chunk<NT, true>(acc[j], ra[j], rb[j], xa16, xb16);
       } else {
-        mma_chunk<NT, false>(acc[0], ra0, rb0, xa, xb);
-        mma_chunk<NT, false>(acc[1], ra1, rb1, xa, xb);
+#pragma unroll
+        for (int j = 0; j < MW; ++j) mma_chunk<NT, false>(acc[j], ra[j], rb[j], xa, xb);
       }
     }
 
@@ -993,9 +1002,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!tile_end) continue;
     if (tcount > 0) named_bar_sync(kBarFree, kConsumerThreads + 32);  // the previous tile's sums have been read
     {
-      float* mine = sRed + (warp * 2 * 32 + lane) * 4 * NT;
+      float* mine = sRed + (warp * MW * 32 + lane) * 4 * NT;
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+      for (int j = 0; j < MW; ++j)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1135,21 +1144,37 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
   return QF_OK;
 }
 
-// Tile shape (BN rows x KS k-bytes per stage).  Longer contiguous runs per weight row stream faster from HBM3e
-// (512-byte runs reach the plain read rate, 128-byte runs about 80 % of it), narrow tiles cost activation copies
-// (2M/BN of the weight bytes) and per-tile epilogues, and too few tiles move work into stream-K splits.  The rule
-// below is the measured best (or within 3 %) on B200 over the Qwen decoder shapes and their 2/4/8-way shards at
-// M = 1, 5 and 16:
-//   N >= ~1.8 x 128 x SMs  (gate_up, vocab head)          -> 128 x 256
-//   N >= ~0.9 x 64 x SMs   (qkv, gate_up shards)          -> 64 x 512
-//   smaller N with N*K >= 5120*8704 (down, its 2-way shard) -> 64 x 512
-//   otherwise (o_proj, narrow shards)                      -> 32 x 1024
-void pick_tiles(int N, int K, int sms, int* bn, int* ks) {
+// Tile shape (BN rows x KS k-bytes per stage) and, for small GEMMs, a data-parallel grid.  Longer contiguous runs
+// per weight row stream faster from HBM3e (512-byte runs reach the plain read rate, 128-byte runs about 80 % of
+// it), narrow tiles cost activation copies (2M/BN of the weight bytes) and per-tile epilogues, and too few tiles
+// move work into stream-K splits, whose cross-CTA reduction (2-4 us of partial-sum stores, counters and reloads)
+// dominates a GEMM of a few MB.  The rule below is the measured best (or within 3 %) on B200 over the Qwen decoder
+// shapes and their 2/4/8-way shards at M = 1, 5 and 16:
+//   a tile height BN in {128, 64, 32} (largest first) giving T = N/BN tiles with SMs/2 <= T <= SMs and at most
+//   160 KiB of weights per tile (320 KiB when T >= 0.9 SMs)   -> BN x (32768/BN), T CTAs of one whole tile each
+//   N >= ~1.8 x 128 x SMs  (gate_up, vocab head)            -> 128 x 256, stream-K
+//   N >= ~0.9 x 64 x SMs   (qkv, gate_up shards)            -> 64 x 512, stream-K
+//   smaller N with N*K >= 5120*6144 (o_proj, down)           -> 64 x 512, stream-K
+//   otherwise (narrow shards)                                -> 32 x 1024, stream-K
+// *dp_grid is the data-parallel grid (0: stream-K over all SMs).
+void pick_tiles(int N, int K, int sms, int* bn, int* ks, int* dp_grid) {
+  *dp_grid = 0;
+  for (int h = 128; h >= 32; h >>= 1) {
+    const long long t = (N + h - 1) / h;
+    const long long bytes = static_cast<long long>(h) * K;
+    const bool fits = bytes <= 160 * 1024 || (10 * t >= 9LL * sms && bytes <= 320 * 1024);
+    if (2 * t >= sms && t <= sms && fits) {
+      *bn = h;
+      *ks = 32768 / h;
+      *dp_grid = static_cast<int>(t);
+      return;
+    }
+  }
   const long long t128 = (N + 127) / 128, t64 = (N + 63) / 64;
   if (10 * t128 >= 18LL * sms) {
     *bn = 128;
     *ks = 256;
-  } else if (10 * t64 >= 9LL * sms || static_cast<long long>(N) * K >= 5120LL * 8704) {
+  } else if (10 * t64 >= 9LL * sms || static_cast<long long>(N) * K >= 5120LL * 6144) {
     *bn = 64;
     *ks = 512;
   } else {
@@ -1193,6 +1218,7 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   const long long total = static_cast<long long>(p.kiters) * p.ntiles;
   int G = dinfo->sm_count;
   if (G > kMaxGrid) G = kMaxGrid;
+  if (p.G > 0 && G > p.G) G = p.G;  // data-parallel grid chosen with the tile shape
   if (grid_cap() > 0 && G > grid_cap()) G = grid_cap();
   if (G > total) G = static_cast<int>(total);
   p.G = G;
@@ -1247,8 +1273,9 @@ const TileShape& tile_override() {
 template <bool HEAD, bool AR = false, bool SILU = false>
 int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
                unsigned flags, cudaStream_t st) {
-  int bn = tile_override().bn, ks = tile_override().ks;
-  if (bn == 0) pick_tiles(p.N, p.K, dinfo->sm_count, &bn, &ks);
+  int bn = tile_override().bn, ks = tile_override().ks, dp_grid = 0;
+  if (bn == 0) pick_tiles(p.N, p.K, dinfo->sm_count, &bn, &ks, &dp_grid);
+  p.G = dp_grid;  // launch() takes it as an upper bound of the grid
   if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
   if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
   if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);

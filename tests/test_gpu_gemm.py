@@ -75,6 +75,8 @@ SHAPES = [
     (19072, 1024, 5, None, None),      # 149 tiles of 128 rows: one stream-K tile shared by 8 CTAs
     (37984, 512, 12, None, None),      # two token tiles, 2 whole tiles per CTA + 1 stream-K tile
     (17024, 256, 3, None, None),       # 64-row tiles
+    (4352, 5120, 5, None, None),       # gate_up shard at TP=8: data-parallel grid, 136 CTAs of one 32-row tile
+    (8704, 5120, 16, None, None),      # gate_up shard at TP=4: data-parallel grid, 136 CTAs of one 64-row tile
 ]
 
 
