@@ -68,6 +68,7 @@ constexpr int kBarFree = 3;                 // epilogue warp -> consumers: sRed 
 constexpr int kBarEnd = 4;                  // consumers + epilogue warp at the end (head only)
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;  // 4 s
 constexpr uint64_t kPeerWaitNs = 100000ull;        // stream-K reducer: wait for the other CTAs' partials (100 us)
+constexpr int kSkSkewStages = 3;                   // default stream-K share skew (stages) when every tile is split
 
 // workspace layout (bytes); the prefix [0, kWsZeroBytes) must be zero before the first call
 constexpr size_t kWsHeader = 256;                              // [0] error flag, [2] CTAs done (head)
@@ -123,6 +124,7 @@ struct Params {
   int r;       // stream-K tiles 0 .. r-1
   int Tsk;     // r * kiters stream-K stages, split over the first Gsk CTAs
   int Gsk;
+  int sk_skew; // q == 0: extra stages of each tile's reducing CTA over the other shares (0: even shares)
   uint8_t* ws;
   int f16_path;
   uint32_t x_tx;  // activation bytes per stage: 2 B boxes of M rows x 128 bytes
@@ -165,12 +167,35 @@ __device__ __forceinline__ RowStat stat_shfl_xor(const RowStat& v, int mask) {
   return o;
 }
 
-__device__ __forceinline__ long long split_start(int c, int T, int G) {
-  return (static_cast<long long>(c) * T) / G;
+// Start of CTA c's stream-K range.  Even shares of the Tsk stages over Gsk CTAs, or, when every tile is split
+// (q == 0, sk_skew = d > 0), uneven shares: each tile's first stage falls in a "long" range of L = S + d stages
+// and the other CTAs get "short" ranges of S stages inside one tile.  A short CTA finishes about d stages before
+// the long ones, so its partial sums are in place when the tile's reducer (the long CTA, whose part of the tile
+// comes last in its range) reaches its end.  With T tiles of K stages over G CTAs: CTA c is long iff
+// c = floor(t G / T) for a tile t, nL = ceil(c T / G) long CTAs precede it, S = T (K - d) / G, and
+// G * start(c) = nL (T K + (G - T) d) + (c - nL) T (K - d), rounded to the nearest stage (the host enables the
+// skew only where G * T * K fits in 31 bits).
+__device__ __forceinline__ int split_start(int c, const Params& p) {
+  if (p.sk_skew == 0) return static_cast<int>((static_cast<long long>(c) * p.Tsk) / p.Gsk);
+  const int T = p.r, K = p.kiters, G = p.Gsk, d = p.sk_skew;
+  const int nl = (c * T + G - 1) / G;
+  const int pos = nl * (T * K + (G - T) * d) + (c - nl) * T * (K - d);
+  return (pos + G / 2) / G;
 }
-// CTA whose (non-empty) range holds iteration i: largest c with split_start(c) <= i (requires G <= T).
-__device__ __forceinline__ int cta_of(int i, int T, int G) {
-  return static_cast<int>(((static_cast<long long>(i) + 1) * G - 1) / T);
+// First and last CTA whose stream-K ranges hold stages of split tile `tile`.
+__device__ __forceinline__ void tile_ctas(int tile, const Params& p, int& c_first, int& c_last) {
+  const long long i0 = static_cast<long long>(tile) * p.kiters;
+  const long long i1 = min(i0 + p.kiters, static_cast<long long>(p.Tsk)) - 1;
+  if (p.sk_skew == 0) {  // the largest c with c * Tsk / Gsk <= i
+    c_first = static_cast<int>(((i0 + 1) * p.Gsk - 1) / p.Tsk);
+    c_last = static_cast<int>(((i1 + 1) * p.Gsk - 1) / p.Tsk);
+    return;
+  }
+  // uneven shares: the tile starts in long CTA floor(tile G / T); its last stages belong to the next tile's long
+  // CTA if that range starts inside this tile, else to the short CTA before it
+  c_first = (tile * p.Gsk) / p.r;
+  const int nxt = ((tile + 1) * p.Gsk) / p.r;
+  c_last = (tile + 1 < p.r && split_start(nxt, p) <= i1) ? nxt : nxt - 1;
 }
 
 __device__ __forceinline__ void record_error(uint8_t* ws, int code) {
@@ -253,8 +278,8 @@ struct StageIter {
   int n_sk, n_iter, sk_begin, sk_end;
   __device__ __forceinline__ void init(const Params& p, int cta) {
     if (cta < p.Gsk) {
-      sk_begin = static_cast<int>(split_start(cta, p.Tsk, p.Gsk));
-      sk_end = static_cast<int>(split_start(cta + 1, p.Tsk, p.Gsk));
+      sk_begin = split_start(cta, p);
+      sk_end = split_start(cta + 1, p);
     } else {
       sk_begin = sk_end = 0;
     }
@@ -403,7 +428,7 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
 #pragma unroll
       for (int uu = 0; uu < U; ++uu) {
         if (cc + uu <= c_last) {
-          const int ft = static_cast<int>(split_start(cc + uu, p.Tsk, p.Gsk) / p.kiters);
+          const int ft = split_start(cc + uu, p) / p.kiters;
           const float4* sl = reinterpret_cast<const float4*>(
               partials + static_cast<size_t>(2 * (cc + uu) + (tile == ft ? 0 : 1)) * kPartialSlotFloats);
 #pragma unroll
@@ -779,6 +804,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         else tc = tt;
       }
     }
+    // CTAs sharing the contributor tile and the reducer tile, kept in shared memory for the tile ends
+    __shared__ int s_tile_ctas[2][2];
+    if (lane == 0) {
+      if (tc >= 0) tile_ctas(tc, p, s_tile_ctas[0][0], s_tile_ctas[0][1]);
+      if (tr >= 0) tile_ctas(tr, p, s_tile_ctas[1][0], s_tile_ctas[1][1]);
+    }
+    __syncwarp();
     uint32_t ar_epoch = 0;  // fused all-reduce: this call's epoch (previous calls on these buffers + 1)
     if constexpr (AR) {
       uint32_t e = 0;
@@ -806,9 +838,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int c_first = 0, c_last = 0;
       if (is_red || is_con) {
-        const int it0 = tile * p.kiters;
-        c_first = cta_of(it0, p.Tsk, p.Gsk);
-        c_last = cta_of(min(it0 + p.kiters, p.Tsk) - 1, p.Tsk, p.Gsk);
+        c_first = s_tile_ctas[is_red ? 1 : 0][0];
+        c_last = s_tile_ctas[is_red ? 1 : 0][1];
       }
       // the tile's sums: the reducer starts from the later CTAs' partials (in CTA order), then adds its own
       float v[MT][NT][4];
@@ -1120,6 +1151,16 @@ int grid_cap() {
   return cap;
 }
 
+// Stream-K share skew in stages (environment QF_SK_SKEW, read once; default kSkSkewStages): how many stages
+// longer the reducing CTA's share of a split tile is than the other shares, when every tile is split.
+int sk_skew_stages() {
+  static const int v = [] {
+    const char* e = std::getenv("QF_SK_SKEW");
+    return e ? std::atoi(e) : kSkSkewStages;
+  }();
+  return v;
+}
+
 // Activation path (environment QF_F16_PATH, read once): 1 (default) converts activations to fp16 for the cheaper
 // exact weight conversion (warps fall back to bf16 where activations leave the fp16 range); 0 keeps bf16.
 int f16_path() {
@@ -1231,6 +1272,13 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   if (gsk > static_cast<long long>(kMaxSplit) * p.r) gsk = static_cast<long long>(kMaxSplit) * p.r;
   p.Gsk = static_cast<int>(gsk);
   if (p.q == 0) p.G = p.Gsk;  // all work is stream-K: CTAs without a share are not launched
+  p.sk_skew = 0;
+  if (p.q == 0 && p.Gsk > p.r && static_cast<long long>(p.Gsk) * p.Tsk < (1LL << 31)) {
+    // every tile split: uneven shares, the short ones keeping at least two stages
+    const int dmax = p.kiters - (2 * p.Gsk + p.r - 1) / p.r;
+    p.sk_skew = sk_skew_stages() < dmax ? sk_skew_stages() : dmax;
+    if (p.sk_skew < 0) p.sk_skew = 0;
+  }
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.G);

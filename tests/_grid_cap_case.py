@@ -1,6 +1,7 @@
-"""Run as ``python -m tests._grid_cap_case`` with QF_GRID_CAP or QF_TILES set: GEMM and head shapes whose
-tiles are split between CTAs in ways the full grid never produces (one CTA, a few CTAs, stream-K shares of many
-stages), or run on a forced tile shape, checked against the oracle.  Exits non-zero on a mismatch.  Used by test_gpu_schedule.py."""
+"""Run as ``python -m tests._grid_cap_case`` with QF_GRID_CAP, QF_TILES or QF_SK_SKEW set: GEMM and head shapes
+whose tiles are split between CTAs in ways the full grid never produces (one CTA, a few CTAs, stream-K shares of
+many stages, even or skewed shares where every tile is split), or run on a forced tile shape, checked against the
+oracle.  Exits non-zero on a mismatch.  Used by test_gpu_schedule.py."""
 from __future__ import annotations
 
 import sys
@@ -15,7 +16,7 @@ def main() -> int:
     from tests.conftest import from_dev_bf16, to_dev_bf16
     from tests.test_gpu_gemm import bf16_close, silu_close
     dev = torch.device("cuda", 0)
-    for (N, K, M) in [(1000, 1024, 5), (10240, 1024, 3), (4100, 2048, 12), (19072, 512, 1)]:
+    for (N, K, M) in [(1000, 1024, 5), (10240, 1024, 3), (4100, 2048, 12), (19072, 512, 1), (2048, 8192, 7)]:
         x, W, s = orc.make_inputs(N + K + M, M, N, K)
         y = w8a16_mm(to_dev_bf16(x, dev), torch.from_numpy(W).to(dev).t(), torch.from_numpy(s).to(dev),
                      pick_config(N, K), torch.bfloat16)
@@ -28,7 +29,7 @@ def main() -> int:
         torch.cuda.synchronize()
         y_orc = orc.w8a16_mm(x, W, s, "bf16")
         silu_close(from_dev_bf16(out), orc.silu_mul(y_orc, I), y_orc, I)
-    for (V, H, M, pad) in [(4100, 2048, 4, 36), (16384 + 640, 1024, 16, 64)]:
+    for (V, H, M, pad) in [(4100, 2048, 4, 36), (16384 + 640, 1024, 16, 64), (3000, 8192, 3, 8)]:
         x, W, s = orc.make_inputs(V + H, M, V, H)
         logits, mx, am, lse = w8a16_head(to_dev_bf16(x, dev), torch.from_numpy(W).to(dev).t(),
                                          torch.from_numpy(s).to(dev), n_valid=V - pad, vocab_offset=0)

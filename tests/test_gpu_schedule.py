@@ -1,6 +1,7 @@
 """Work schedules and kernel instances the default choice does not reach: the grid capped to 1, 5 and 37 CTAs
-(environment QF_GRID_CAP) and every tile shape BN:KS forced (environment QF_TILES).  Both are read once per
-process, so each setting runs in a child process that checks GEMM and head results against the oracle."""
+(environment QF_GRID_CAP), every tile shape BN:KS forced (environment QF_TILES), and even or differently skewed
+stream-K shares where every tile is split (environment QF_SK_SKEW).  All are read once per process, so each
+setting runs in a child process that checks GEMM and head results against the oracle."""
 from __future__ import annotations
 
 import os
@@ -13,20 +14,23 @@ import pytest
 pytestmark = pytest.mark.gpu
 REPO = Path(__file__).resolve().parent.parent
 
-SETTINGS = [("1", ""), ("5", ""), ("37", ""),
-            ("", "128:128"), ("", "128:256"), ("", "64:256"), ("", "64:512"), ("", "32:512"), ("", "32:1024"),
-            ("5", "128:256"), ("37", "32:1024")]
+SETTINGS = [("1", "", ""), ("5", "", ""), ("37", "", ""),
+            ("", "128:128", ""), ("", "128:256", ""), ("", "64:256", ""), ("", "64:512", ""), ("", "32:512", ""),
+            ("", "32:1024", ""), ("5", "128:256", ""), ("37", "32:1024", ""),
+            ("", "", "0"), ("", "", "1"), ("", "", "7"), ("100", "64:512", "5")]
 
 
-@pytest.mark.parametrize("cap,tiles", SETTINGS, ids=lambda v: v or "-")
-def test_schedules_and_tile_shapes_match_oracle(dev, cap, tiles):
+@pytest.mark.parametrize("cap,tiles,skew", SETTINGS, ids=lambda v: v or "-")
+def test_schedules_and_tile_shapes_match_oracle(dev, cap, tiles, skew):
     env = dict(os.environ)
-    env.pop("QF_GRID_CAP", None)
-    env.pop("QF_TILES", None)
+    for k in ("QF_GRID_CAP", "QF_TILES", "QF_SK_SKEW"):
+        env.pop(k, None)
     if cap:
         env["QF_GRID_CAP"] = cap
     if tiles:
         env["QF_TILES"] = tiles
+    if skew:
+        env["QF_SK_SKEW"] = skew
     r = subprocess.run([sys.executable, "-m", "tests._grid_cap_case"], cwd=REPO, env=env, capture_output=True,
                        text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
