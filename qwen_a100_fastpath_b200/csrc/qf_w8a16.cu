@@ -66,6 +66,7 @@ constexpr int kBarConsumers = 1;            // named barriers (0 is __syncthread
 constexpr int kBarReady = 2;                // consumers -> epilogue warp: a tile's partial sums are in sRed
 constexpr int kBarFree = 3;                 // epilogue warp -> consumers: sRed has been read
 constexpr int kBarEnd = 4;                  // consumers + epilogue warp at the end (head only)
+constexpr int kBarCoop = 5;                 // epilogue warp -> consumers: peers' partial sums staged for the last tile
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;  // 4 s
 constexpr uint64_t kPeerWaitNs = 100000ull;        // stream-K reducer: wait for the other CTAs' partials (100 us)
 constexpr int kSkSkewStages = 3;                   // default stream-K share skew (stages) when every tile is split
@@ -630,6 +631,78 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
   }
 }
 
+// The CTA's last tile, finished by the eight consumer warps together instead of the epilogue warp alone (nothing is
+// left to overlap with it, so it sits on the launch's critical path): warp w sums m-tiles w, w + 8, ... from the
+// warps' partial sums in sRed -- starting from the stream-K peers' sums in sPeer when `peers` -- in the epilogue
+// warp's order, so the bits are the same as finish_tile's, then all consumers store the staged rows.
+// Plain GEMM instances with bf16 output only.
+template <int BN, int NT, int MW, int NMW>
+__device__ __forceinline__ void coop_finish_tile(const Params& p, int tile, int warp, const float* sRed,
+                                                 const float* sPeer, bool peers, __nv_bfloat16* sOut) {
+  constexpr int MT = BN / 16;
+  constexpr int OS = BN + 8;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  for (int mt = warp; mt < MT; mt += kConsumerWarps) {
+    float v[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[nt][e] = peers ? sPeer[(mt * 32 + lane) * 4 * NT + nt * 4 + e] : 0.f;
+#pragma unroll
+    for (int bb = 0; bb < 4 / NMW; ++bb)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int src = 2 * (bb * NMW + mt / MW) + hh;
+        const float* o = sRed + ((src * MW + mt % MW) * 32 + lane) * 4 * NT;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[nt][e] += o[nt * 4 + e];
+      }
+    const int n0 = tile * BN + 16 * mt + g;
+    const int n1 = n0 + 8;
+    const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
+    const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
+    float b0 = 0.f, b1 = 0.f;
+    if (p.bias) {
+      if (n0 < p.N) b0 = __bfloat162float(p.bias[n0]);
+      if (n1 < p.N) b1 = __bfloat162float(p.bias[n1]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int bq = 0; bq < 2; ++bq) {
+        const int m = 8 * nt + 2 * t + bq;
+        __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][bq] * s0);
+        __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + bq] * s1);
+        if (p.bias) {
+          r0 = __float2bfloat16_rn(__bfloat162float(r0) + b0);
+          r1 = __float2bfloat16_rn(__bfloat162float(r1) + b1);
+        }
+        sOut[m * OS + 16 * mt + g] = r0;
+        sOut[m * OS + 16 * mt + g + 8] = r1;
+      }
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  constexpr int CH = BN / 8;
+  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.y);
+  for (int idx = threadIdx.x; idx < p.M * CH; idx += kConsumerThreads) {
+    const int m = idx / CH;
+    const int ch = idx - m * CH;
+    const int n = tile * BN + ch * 8;
+    const __nv_bfloat16* src = sOut + m * OS + ch * 8;
+    __nv_bfloat16* out = dst + static_cast<int64_t>(m) * p.ldy + n;
+    if (p.out_vec && n + 8 <= p.N) {
+      *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+    } else {
+      for (int e = 0; e < 8; ++e)
+        if (n + e < p.N) out[e] = src[e];
+    }
+  }
+}
+
 // Head: folds a finished tile's per-token statistics (sTile[m], written by the epilogue warp) into lane m's running
 // statistics of this CTA, in the order the CTA finishes its tiles.
 __device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTile, RowStat& run) {
@@ -664,6 +737,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty_bar = full_bar + S;                                   // all consumer warps read the stage
   volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffFlag);
   volatile int* sLast = sAbort + 1;
+  volatile int* sCoop = sAbort + 2;  // last tile: 0 epilogue warp finishes it, 1 consumers, 2 consumers + peers' sums
+  // the CTA's last tile is finished by the consumer warps (plain GEMM instances with bf16 output)
+  constexpr bool kCoopLast = !HEAD && !AR && !SILU;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -676,6 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     *sAbort = 0;
     *sLast = 0;
+    *sCoop = 0;
     fence_mbar_init();
   }
   {
@@ -886,7 +963,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      const bool coop_tile = kCoopLast && !p.y_f32 && tcount == n_ends - 1;
+      const bool coop = coop_tile && !is_con && (!is_red || red_ok);
+      if (coop_tile) {
+        if (lane == 0) *sCoop = coop ? (is_red ? 2 : 1) : 0;
+        __syncwarp();
+      }
       named_bar_sync(kBarReady, kConsumerThreads + 32);
+      if (coop) {
+        // the consumers finish the tile; the weight ring is idle now (every stage consumed): stage the peers' sums
+        // there in the consumers' accumulator layout
+        if (is_red) {
+          float* sPeer = reinterpret_cast<float*>(sW);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) sPeer[(mt * 32 + lane) * 4 * NT + nt * 4 + e] = v[mt][nt][e];
+          named_bar_arrive(kBarCoop, kConsumerThreads + 32);
+          if (lane == 0) counters[tile] = 0;  // every other contributor has counted itself in: re-arm
+        }
+        ++tcount;
+        continue;
+      }
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -1029,6 +1129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ------------------------------------------------------------ tile end: hand the sums to the epilogue warp
     const bool tile_end = (it.kk == p.kiters - 1) || (it.sk && i == it.n_sk - 1);
+    const int cur_tile = it.tile;
     it.next(p);
     if (!tile_end) continue;
     if (tcount > 0) named_bar_sync(kBarFree, kConsumerThreads + 32);  // the previous tile's sums have been read
@@ -1044,7 +1145,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[j][nt][e] = 0.f;
           }
     }
-    named_bar_arrive(kBarReady, kConsumerThreads + 32);
+    if (kCoopLast && !p.y_f32 && i == n_iter - 1) {  // the CTA's last tile: finished here unless the epilogue
+      named_bar_sync(kBarReady, kConsumerThreads + 32);  // warp keeps it (stream-K contribution)
+      const int mode = *sCoop;
+      if (mode == 2) named_bar_sync(kBarCoop, kConsumerThreads + 32);
+      if (mode != 0)
+        coop_finish_tile<BN, NT, MW, NMW>(p, cur_tile, warp, sRed, reinterpret_cast<const float*>(sW), mode == 2,
+                                          sOut);
+    } else {
+      named_bar_arrive(kBarReady, kConsumerThreads + 32);
+    }
     ++tcount;
   }
 
