@@ -514,15 +514,16 @@ def run_sweep(args, local: int):
     """Config 4: every config-2 GEMM and the head at M in {1,2,3,4,5,8,12,16}, timed alone (CUDA graph of 64
     launches over distinct weights, so every launch streams from HBM)."""
     import torch
-    from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_mm
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_head_sample, w8a16_mm
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peak, _ = peak_hbm()
     g = torch.Generator(device=dev).manual_seed(7)
     rows = []
     stream = torch.cuda.Stream(dev)
-    for name, N, K, _ in LAYER + [HEAD]:
-        copies = 64 if name != "lm_head" else 4
+    for name, N, K, _ in LAYER + [HEAD, ("lm_head_sample",) + tuple(HEAD[1:])]:
+        head = name.startswith("lm_head")
+        copies = 64 if not head else 4
         Ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g) for _ in range(copies)]
         Ss = [torch.rand(N, device=dev, generator=g) * 0.009 + 0.001 for _ in range(copies)]
         for M in (1, 2, 3, 4, 5, 8, 12, 16):
@@ -534,6 +535,8 @@ def run_sweep(args, local: int):
             def call(i):
                 if name == "lm_head":
                     w8a16_head(x, Ws[i].t(), Ss[i], pdl=True, out=outs)
+                elif name == "lm_head_sample":  # the fused temperature draw (probabilistic drafting)
+                    w8a16_head_sample(x, Ws[i].t(), Ss[i], temperature=0.8, seed=1, offset=i, pdl=True)
                 else:
                     w8a16_mm(x, Ws[i].t(), Ss[i], None, torch.bfloat16, out=y, pdl=True)
 
@@ -542,12 +545,12 @@ def run_sweep(args, local: int):
                     call(i)
             torch.cuda.synchronize()
             gr = torch.cuda.CUDAGraph()
-            reps = 64 if name != "lm_head" else 16
+            reps = 64 if not head else 16
             with torch.cuda.graph(gr, stream=stream):
                 for i in range(reps):
                     call(i % copies)
             ms = time_graph(gr, stream, 5, 2) / reps
-            b = alg_bytes(N, K, M, head=name == "lm_head")
+            b = alg_bytes(N, K, M, head=head)
             gbs = b / (ms * 1e-3) / 1e9
             rows.append({"gemm": name, "N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "GBps": round(gbs, 1),
                          "frac_measured": round(gbs / peak, 4), "frac_nominal": round(gbs / NOMINAL_HBM_GBS, 4)})

@@ -86,6 +86,23 @@ int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
                   float* row_max, int64_t* row_argmax, float* row_lse,
                   void* ws, size_t ws_bytes, unsigned flags, void* stream);
 
+/* Int8 draft head with a fused temperature draw for probabilistic drafting (no counterpart in the reference,
+ * whose draft head is greedy only, patches.py:176-185).  Same GEMM and logits as qf_w8a16_head; the statistics
+ * are of the scaled logits s = logit * inv_temperature (row_max, row_argmax, row_lse = logsumexp(s)), and each
+ * row also gets one Gumbel-max draw from softmax(s) over columns [0, n_valid):
+ *   row_sample = argmax_j s_j + g_j (+ vocab_offset), row_sample_score = that maximum, row_sample_logit = s at it,
+ *   g_j = -log(-log u), u = ((word >> 9) + 1/2) * 2^-23, word = Philox4x32-10 (Salmon et al., SC 2011) of the
+ *   counter (j + vocab_offset, m / 4, offset low, offset high) under the key (seed low, seed high), word m % 4.
+ * The draft probability of the draw is exp(row_sample_logit - row_lse).  The noise depends only on (seed, offset,
+ * global column, row), so vocab shards draw exactly what one unsharded head draws: take the shard with the
+ * largest row_sample_score (lowest column on ties) and combine row_lse as for qf_w8a16_head.
+ * inv_temperature finite and > 0; vocab_offset + N <= 2^32. */
+int qf_w8a16_head_sample(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
+                         void* logits, int64_t ldl, int M, int N, int K, int n_valid, int64_t vocab_offset,
+                         float inv_temperature, uint64_t seed, uint64_t offset, float* row_max,
+                         int64_t* row_argmax, float* row_lse, int64_t* row_sample, float* row_sample_score,
+                         float* row_sample_logit, void* ws, size_t ws_bytes, unsigned flags, void* stream);
+
 /* Small-M W8A16 GEMM that allocates nothing and takes no workspace.  No counterpart in the reference: it is
  * for callers that cannot allocate device memory themselves -- a host that embeds only this library through
  * the C ABI (a Go, Java or C binding with no device allocator of its own), or a latency-critical path that

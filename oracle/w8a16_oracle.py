@@ -18,6 +18,9 @@ It restates, in numpy, the arithmetic of EurekaZang/qwen-a100-fastpath's ``qwen_
 * ``top_tokens`` / ``head_stats`` -- ``get_top_tokens`` (patches.py:182-185: padding columns to -inf,
   first-index argmax, + vocab start offset) and the fused per-row (max, argmax, logsumexp) over the
   same bf16 logits.
+* ``head_sample``         -- the fused temperature draw for probabilistic drafting (no reference
+  counterpart: the reference drafts greedily): Gumbel-max over the scaled bf16 logits with
+  Philox4x32-10 noise (``philox4x32_10``, pinned by the generator's published known-answer vectors).
 
 Parity is pinned: ``tests/golden/make_fixtures.py`` ran the reference's own ``w8a16_mm``,
 ``qf_int8_linear`` and draft-head patches (Triton interpreter, with two interpreter bf16 bugs fixed) and
@@ -201,6 +204,85 @@ def head_stats(logits_bits, n_valid: int, vocab_offset: int = 0):
     am = np.argmax(v, axis=1).astype(np.int64) + int(vocab_offset)
     lse = mx + np.log(np.exp(v - mx[:, None]).sum(axis=1))
     return mx.astype(np.float32), am, lse
+
+
+_PHILOX_M = (0xD2511F53, 0xCD9E8D57)
+_PHILOX_W = (0x9E3779B9, 0xBB67AE85)
+
+
+def philox4x32_10(ctr, key):
+    """Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011).
+
+    ``ctr``: uint32 array [..., 4]; ``key``: two uint32.  Ten rounds of
+    ``(c0, c1, c2, c3) -> (hi(M1*c2) ^ c1 ^ k0, lo(M1*c2), hi(M0*c0) ^ c3 ^ k1, lo(M0*c0))`` with the key advanced
+    by the Weyl constants between rounds.  Checked against the generator's published known-answer vectors in
+    ``tests/test_oracle_golden.py``.  Returns uint32 [..., 4].
+    """
+    c = np.asarray(ctr, dtype=np.uint64) & np.uint64(0xFFFFFFFF)
+    c0, c1, c2, c3 = (c[..., i].copy() for i in range(4))
+    k0, k1 = np.uint64(key[0] & 0xFFFFFFFF), np.uint64(key[1] & 0xFFFFFFFF)
+    mask = np.uint64(0xFFFFFFFF)
+    for r in range(10):
+        p0 = np.uint64(_PHILOX_M[0]) * c0
+        p1 = np.uint64(_PHILOX_M[1]) * c2
+        c0, c1, c2, c3 = ((p1 >> np.uint64(32)) ^ c1 ^ k0) & mask, p1 & mask, \
+            ((p0 >> np.uint64(32)) ^ c3 ^ k1) & mask, p0 & mask
+        if r < 9:
+            k0 = (k0 + np.uint64(_PHILOX_W[0])) & mask
+            k1 = (k1 + np.uint64(_PHILOX_W[1])) & mask
+    return np.stack([c0, c1, c2, c3], axis=-1).astype(np.uint32)
+
+
+def gumbel_noise(M: int, cols, seed: int, offset: int) -> np.ndarray:
+    """Gumbel noise g[m, j] (fp64) of the fused draft draw for rows m < M and global columns ``cols``: the word
+    ``m % 4`` of Philox4x32-10 with counter (column, m // 4, offset low, offset high) and key (seed low, seed high),
+    u = ((word >> 9) + 1/2) * 2^-23 (exact in fp32), g = -log(-log u)."""
+    cols = np.asarray(cols, dtype=np.uint64)
+    q = np.arange((M + 3) // 4, dtype=np.uint64)
+    ctr = np.zeros((len(q), len(cols), 4), dtype=np.uint64)
+    ctr[..., 0] = cols[None, :]
+    ctr[..., 1] = q[:, None]
+    ctr[..., 2] = offset & 0xFFFFFFFF
+    ctr[..., 3] = (offset >> 32) & 0xFFFFFFFF
+    words = philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))  # [quads, cols, 4]
+    words = np.transpose(words, (0, 2, 1)).reshape(-1, len(cols))[:M]             # row m = 4 q + e
+    u = ((words >> np.uint32(9)).astype(np.float64) + 0.5) * 2.0 ** -23
+    return -np.log(-np.log(u))
+
+
+def head_sample(logits_bits, n_valid: int, inv_temp: float, seed: int, offset: int, vocab_offset: int = 0):
+    """Fused temperature draw of the draft head (``qf_w8a16_head_sample``) on bf16 logits [M, V].
+
+    s = fp32(logit) * fp32(inv_temp) (one fp32 rounding, as the kernel); statistics (max, argmax + offset,
+    logsumexp in fp64) of s over columns < n_valid; Gumbel-max draw argmax_j s_j + g[m, j + vocab_offset] (first
+    column on ties).  Returns (max fp32, argmax int64, lse fp64, sample int64, score fp64, sample logit fp32,
+    margin fp64 = best minus second-best perturbed score, for tolerance decisions)."""
+    l = bf16_to_f32(logits_bits)[:, :n_valid]
+    sv = (l * np.float32(inv_temp)).astype(np.float32)
+    M = sv.shape[0]
+    mx = sv.max(axis=1)
+    am = np.argmax(sv, axis=1).astype(np.int64) + int(vocab_offset)
+    s64 = sv.astype(np.float64)
+    lse = s64.max(axis=1) + np.log(np.exp(s64 - s64.max(axis=1, keepdims=True)).sum(axis=1))
+    z = s64 + gumbel_noise(M, np.arange(n_valid, dtype=np.int64) + int(vocab_offset), seed, offset)
+    smp = np.argmax(z, axis=1)
+    zs = np.sort(z, axis=1)
+    margin = zs[:, -1] - zs[:, -2] if n_valid > 1 else np.full(M, np.inf)
+    return (mx, am, lse, smp.astype(np.int64) + int(vocab_offset), z[np.arange(M), smp],
+            sv[np.arange(M), smp], margin)
+
+
+def combine_head_samples(parts):
+    """Merge per-shard draws (score [M], global column [M], logit [M]) of a vocab-sharded head: the largest score
+    wins, lowest column on ties -- equal to the unsharded draw because the noise is keyed by the global column."""
+    sc = np.stack([np.asarray(p[0], np.float64) for p in parts])
+    col = np.stack([np.asarray(p[1], np.int64) for p in parts])
+    lg = np.stack([np.asarray(p[2], np.float64) for p in parts])
+    best = sc.max(axis=0)
+    cand = np.where(sc == best[None, :], col, np.iinfo(np.int64).max)
+    pick = cand.min(axis=0)
+    which = np.argmax((col == pick[None, :]) & (sc == best[None, :]), axis=0)
+    return pick, lg[which, np.arange(sc.shape[1])]
 
 
 def top2_gap(logits_bits, n_valid: int) -> np.ndarray:

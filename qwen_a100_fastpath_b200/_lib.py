@@ -34,6 +34,10 @@ SIGNATURES = [
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int,
       _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
       _c.c_size_t, _c.c_uint, _c.c_void_p]),
+    ("qf_w8a16_head_sample", _c.c_int,
+     [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int,
+      _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.c_float, _c.c_uint64, _c.c_uint64, _c.c_void_p, _c.c_void_p,
+      _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t, _c.c_uint, _c.c_void_p]),
     ("qf_w8a16_gemm_noalloc", _c.c_int,
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64,
       _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_uint, _c.c_void_p]),

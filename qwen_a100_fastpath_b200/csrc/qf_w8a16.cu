@@ -78,7 +78,8 @@ constexpr size_t kWsZeroBytes = kWsCounters + sizeof(int) * kMaxTiles;
 constexpr size_t kWsPartials = (kWsZeroBytes + 1023) / 1024 * 1024;
 constexpr size_t kPartialSlotFloats = kMaxBN * 16;              // [BN rows][8*NT tokens]
 constexpr size_t kWsCtaStats = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kMaxGrid;  // head
-constexpr size_t kWsBytes = kWsCtaStats + sizeof(float4) * 16 * kMaxGrid;  // float4 [16 tokens][kMaxGrid CTAs]
+constexpr size_t kWsCtaDraws = kWsCtaStats + sizeof(float4) * 16 * kMaxGrid;  // float4 [16 tokens][kMaxGrid CTAs]
+constexpr size_t kWsBytes = kWsCtaDraws + sizeof(float4) * 16 * kMaxGrid;     // head draws, same layout
 
 template <int BN, int NT, int KS> struct Geo {
   static constexpr int B = KS / 128;                            // 128-byte weight boxes per stage
@@ -142,6 +143,13 @@ struct Params {
   float* row_max;
   long long* row_argmax;
   float* row_lse;
+  // head: the statistics are of the scaled logits s = logit * inv_temp (1 for the greedy head); the drawing head
+  // instance (HEAD == 2) also makes a Gumbel-max draw from softmax(s) per row: argmax_j s_j + g(seed, offset, j, m)
+  float inv_temp;
+  uint32_t seed_lo, seed_hi, off_lo, off_hi;
+  long long* row_sample;
+  float* row_sample_score;
+  float* row_sample_logit;
 };
 
 struct RowStat {
@@ -158,6 +166,50 @@ __device__ __forceinline__ RowStat stat_combine(const RowStat& x, const RowStat&
   const float sy = (y.m == -INFINITY) ? 0.f : y.s * expf(y.m - r.m);
   r.s = sx + sy;
   return r;
+}
+
+// Gumbel-max draw: the largest perturbed score z = s + g, its column (smaller column on ties) and its s.
+struct SampleArg {
+  float z;
+  int a;
+  float s;
+};
+__device__ __forceinline__ SampleArg sa_max(const SampleArg& x, const SampleArg& y) {
+  return (y.z > x.z || (y.z == x.z && y.a < x.a)) ? y : x;
+}
+__device__ __forceinline__ SampleArg sa_shfl_xor(const SampleArg& v, int mask) {
+  return SampleArg{__shfl_xor_sync(0xffffffffu, v.z, mask), __shfl_xor_sync(0xffffffffu, v.a, mask),
+                   __shfl_xor_sync(0xffffffffu, v.s, mask)};
+}
+
+// Philox4x32-10 counter-based generator (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3",
+// SC 2011): ten rounds of two 32x32 -> 64-bit products, with a Weyl key schedule between rounds.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// Random words of (global column j, tokens 4q .. 4q + 3) for this draw: Philox4x32-10 of the counter
+// (j, q, offset lo, offset hi) under the key (seed lo, seed hi); word e belongs to token 4q + e.
+__device__ __forceinline__ uint4 draw_words(const Params& p, long long j, int q) {
+  return philox4x32_10(make_uint4(static_cast<uint32_t>(j), static_cast<uint32_t>(q), p.off_lo, p.off_hi), p.seed_lo,
+                       p.seed_hi);
+}
+
+// Standard Gumbel noise from a random word: u = (w >> 9 + 1/2) * 2^-23, exact in fp32, in (0, 1); g = -log(E),
+// E = -log(u) ~ Exp(1).  The inner logarithm needs full precision (for u near 1, -log u is tiny and an absolute
+// error would dominate it); the outer one takes the fast approximation (E >= 6e-8: its absolute error in g is
+// below 1e-5, far under the spacing of competing perturbed scores that matters for the draw).
+__device__ __forceinline__ float gumbel_of(uint32_t w) {
+  const float u = (static_cast<float>(w >> 9) + 0.5f) * 1.1920928955078125e-07f;
+  return -__logf(-logf(u));
 }
 
 __device__ __forceinline__ RowStat stat_shfl_xor(const RowStat& v, int mask) {
@@ -406,7 +458,7 @@ __device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int
 // Reduction of a stream-K tile from every contributor's slot (CTAs c_first .. c_last, in that order), by the
 // contributor that arrived last when the tile's designated reducer did not wait for the others: finishes the tile
 // (scale + store, or logits + tile statistics for the head) and re-arms the tile's counter.
-template <int BN, int NT, bool HEAD, bool AR, bool SILU>
+template <int BN, int NT, int HEAD, bool AR, bool SILU>
 __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int lane, int c_first, int c_last,
                                                  int* counters, const float* partials, float4* sTile,
                                                  __nv_bfloat16* sOut, uint32_t ar_epoch) {
@@ -419,6 +471,7 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
   constexpr int U = PC >= 8 ? 1 : 8 / PC;  // contributors whose loads are in flight together
   const int m_base = 4 * (lane % (2 * NT));
   RowStat st[4];
+  SampleArg sz[4];  // head with sampling: Gumbel-max draw per token m_base + e
 #pragma unroll
   for (int pass = 0; pass < PER / PC; ++pass) {
     float4 v[PC];
@@ -456,6 +509,8 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
       const int n = wr < 0 ? p.N : wr;  // past the end: masked below
       const float sc = wr >= 0 ? __ldg(p.scale + wr) : 0.f;
       const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      uint4 wd = make_uint4(0u, 0u, 0u, 0u);  // head with sampling: noise words of (row, tokens m_base ..)
+      if (HEAD == 2 && n < p.n_valid) wd = draw_words(p, n + p.vocab_offset, m_base / 4);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int m = m_base + e;
@@ -467,9 +522,14 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
         } else {
           const __nv_bfloat16 rv = __float2bfloat16_rn(vv[e] * sc);
           if (p.logits && m < p.M && n < p.N) p.logits[static_cast<int64_t>(m) * p.ldl + n] = rv;
-          const RowStat one =
-              n < p.n_valid ? RowStat{__bfloat162float(rv), n, 1.f} : RowStat{-INFINITY, INT_MAX, 0.f};
+          const float sv = HEAD == 2 ? __bfloat162float(rv) * p.inv_temp : __bfloat162float(rv);
+          const RowStat one = n < p.n_valid ? RowStat{sv, n, 1.f} : RowStat{-INFINITY, INT_MAX, 0.f};
           st[e] = (pass == 0 && j == 0) ? one : stat_combine(st[e], one);
+          if constexpr (HEAD == 2) {
+            const uint32_t u = e == 0 ? wd.x : e == 1 ? wd.y : e == 2 ? wd.z : wd.w;
+            const SampleArg z1 = n < p.n_valid ? SampleArg{sv + gumbel_of(u), n, sv} : SampleArg{-INFINITY, INT_MAX, 0.f};
+            sz[e] = (pass == 0 && j == 0) ? z1 : sa_max(sz[e], z1);
+          }
         }
       }
     }
@@ -482,6 +542,12 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
       for (int off = 2 * NT; off < 32; off <<= 1) sr = stat_combine(sr, stat_shfl_xor(sr, off));
       if (lane < 2 * NT)
         sTile[m_base + e] = make_float4(sr.m, __int_as_float(sr.a), sr.s, 0.f);
+      if constexpr (HEAD == 2) {
+        SampleArg zr = sz[e];
+#pragma unroll
+        for (int off = 2 * NT; off < 32; off <<= 1) zr = sa_max(zr, sa_shfl_xor(zr, off));
+        if (lane < 2 * NT) sTile[16 + m_base + e] = make_float4(zr.z, __int_as_float(zr.a), zr.s, 0.f);
+      }
     }
   }
   if constexpr (AR) {
@@ -499,7 +565,7 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
 // tokens 8 nt + 2 t and 8 nt + 2 t + 1): scale, bf16 rounding (+ the bias as a second rounding), rows staged in
 // shared memory and written with 16-byte stores (GEMM output or head logits), and for the head the tile's per-token
 // (max, first argmax, sum exp) of its bf16 logits.
-template <int BN, int NT, bool HEAD, bool AR, bool SILU>
+template <int BN, int NT, int HEAD, bool AR, bool SILU>
 __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane, const float (&v)[BN / 16][NT][4],
                                             const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* sTile,
                                             uint32_t ar_epoch) {
@@ -525,6 +591,7 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
     }
   }
   MaxArg mx[NT][2];  // head: per token 8 nt + 2 t + bq over this lane's rows
+  const float inv_t = HEAD == 2 ? p.inv_temp : 1.0f;  // the greedy head's statistics are of the logits themselves
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -553,8 +620,8 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
             r1 = __float2bfloat16_rn(__bfloat162float(r1) + b1);
           }
         } else {
-          if (n0 < p.n_valid) mx[nt][bq] = ma_max(mx[nt][bq], MaxArg{__bfloat162float(r0), n0});
-          if (n1 < p.n_valid) mx[nt][bq] = ma_max(mx[nt][bq], MaxArg{__bfloat162float(r1), n1});
+          if (n0 < p.n_valid) mx[nt][bq] = ma_max(mx[nt][bq], MaxArg{__bfloat162float(r0) * inv_t, n0});
+          if (n1 < p.n_valid) mx[nt][bq] = ma_max(mx[nt][bq], MaxArg{__bfloat162float(r1) * inv_t, n1});
         }
         sOut[m * OS + 16 * mt + g] = r0;
         sOut[m * OS + 16 * mt + g + 8] = r1;
@@ -610,8 +677,8 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
         for (int bq = 0; bq < 2; ++bq) {
           const float mref = mx[nt][bq].m;
           if (mref != -INFINITY) {
-            const float r0 = __bfloat162float(__float2bfloat16_rn(v[mt][nt][bq] * sc[mt][0]));
-            const float r1 = __bfloat162float(__float2bfloat16_rn(v[mt][nt][2 + bq] * sc[mt][1]));
+            const float r0 = __bfloat162float(__float2bfloat16_rn(v[mt][nt][bq] * sc[mt][0])) * inv_t;
+            const float r1 = __bfloat162float(__float2bfloat16_rn(v[mt][nt][2 + bq] * sc[mt][1])) * inv_t;
             if (n0 < p.n_valid) se[nt][bq] += expf(r0 - mref);
             if (n1 < p.n_valid) se[nt][bq] += expf(r1 - mref);
           }
@@ -628,6 +695,63 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
         if (g == 0)
           sTile[8 * nt + 2 * t + bq] = make_float4(mx[nt][bq].m, __int_as_float(mx[nt][bq].a), sum, 0.f);
       }
+    if constexpr (HEAD == 2) {
+      // Gumbel-max draw over the tile's logits as staged in sOut: lane l takes rows l, l + 32, ...; one Philox call
+      // per (row, token quad) gives the noise of four tokens; z = s + g, then the best z per token over the warp.
+      // The noise lies in [-2.81, 16.64] (u in [2^-24, 1 - 2^-24]), so a logit more than 19.45 below the tile's
+      // largest s can never beat that element's z: its noise is not drawn (an exact pruning; kDrawPrune = 20.5
+      // leaves room for rounding).
+      constexpr float kDrawPrune = 20.5f;
+      int* sList = reinterpret_cast<int*>(sTile + 32);  // candidate rows of the tile (BN ints, after the statistics)
+      __syncwarp();  // the tile maxima of s (sTile[m].x) written above
+      for (int q = 0; 4 * q < p.M; ++q) {
+        float thr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)  // padded token rows draw nothing
+          thr[e] = 4 * q + e < p.M ? sTile[4 * q + e].x - kDrawPrune : INFINITY;
+        // candidates: rows holding a logit within kDrawPrune of its token's tile maximum, compacted so that the
+        // Philox calls and logarithms run on full warps
+        int cnt = 0;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) {
+          const int r = lane + 32 * i;
+          bool need = false;
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            need |= __bfloat162float(sOut[(4 * q + e) * OS + r]) * p.inv_temp >= thr[e];
+          need = need && tile * BN + r < p.n_valid;
+          const uint32_t mask = __ballot_sync(0xffffffffu, need);
+          if (need) sList[cnt + __popc(mask & ((1u << lane) - 1u))] = r;
+          cnt += __popc(mask);
+        }
+        __syncwarp();
+        SampleArg best[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) best[e] = SampleArg{-INFINITY, INT_MAX, 0.f};
+        for (int c = lane; c < cnt; c += 32) {
+          const int r = sList[c];
+          const int n = tile * BN + r;
+          const uint4 w = draw_words(p, n + p.vocab_offset, q);
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float sv = __bfloat162float(sOut[(4 * q + e) * OS + r]) * p.inv_temp;
+            if (sv >= thr[e]) best[e] = sa_max(best[e], SampleArg{sv + gumbel_of(wv[e]), n, sv});
+          }
+        }
+        const int ne = p.M - 4 * q < 4 ? p.M - 4 * q : 4;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (e < ne) {
+            SampleArg b = best[e];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) b = sa_max(b, sa_shfl_xor(b, off));
+            if (lane == 0) sTile[16 + 4 * q + e] = make_float4(b.z, __int_as_float(b.a), b.s, 0.f);
+          }
+        }
+        __syncwarp();  // sList is rewritten for the next quad
+      }
+    }
   }
 }
 
@@ -705,16 +829,21 @@ __device__ __forceinline__ void coop_finish_tile(const Params& p, int tile, int 
 
 // Head: folds a finished tile's per-token statistics (sTile[m], written by the epilogue warp) into lane m's running
 // statistics of this CTA, in the order the CTA finishes its tiles.
-__device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTile, RowStat& run) {
+template <int HEAD>
+__device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTile, RowStat& run, SampleArg& run_z) {
   __syncwarp();
   if (lane < p.M) {
     const float4 f = sTile[lane];
     run = stat_combine(run, RowStat{f.x, __float_as_int(f.y), f.z});
+    if constexpr (HEAD == 2) {
+      const float4 z = sTile[16 + lane];
+      run_z = sa_max(run_z, SampleArg{z.x, __float_as_int(z.y), z.z});
+    }
   }
   __syncwarp();
 }
 
-template <int BN, int NT, int KS, bool HEAD, bool AR, bool SILU>
+template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  const Params p) {
@@ -854,6 +983,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* counters = reinterpret_cast<int*>(p.ws + kWsCounters);
   float* partials = reinterpret_cast<float*>(p.ws + kWsPartials);
   float4* cta_stats = reinterpret_cast<float4*>(p.ws + kWsCtaStats);
+  float4* cta_draws = reinterpret_cast<float4*>(p.ws + kWsCtaDraws);
   // tile ends of this CTA: every tile its stream-K range touches, then its q whole tiles
   const int n_ends = (it.n_sk > 0 ? sk_t1 - sk_t0 + 1 : 0) + p.q;
 
@@ -897,6 +1027,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     StageIter et = it;
     int tcount = 0;
     RowStat run{-INFINITY, INT_MAX, 0.f};  // head: lane m folds token m's statistics over this CTA's tiles
+    SampleArg run_z{-INFINITY, INT_MAX, 0.f};  // head with sampling: lane m's draw over this CTA's tiles
     for (int i = 0; i < n_iter; ++i) {
       const int tile = et.tile;
       const bool sk = et.sk;
@@ -1027,12 +1158,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           split_reduce_all<BN, NT, HEAD, AR, SILU>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut, ar_epoch);
-          if constexpr (HEAD) fold_tile(p, lane, sStat, run);
+          if constexpr (HEAD) fold_tile<HEAD>(p, lane, sStat, run, run_z);
         }
         continue;
       }
       finish_tile<BN, NT, HEAD, AR, SILU>(p, tile, lane, v, sc, sOut, sStat, ar_epoch);
-      if constexpr (HEAD) fold_tile(p, lane, sStat, run);
+      if constexpr (HEAD) fold_tile<HEAD>(p, lane, sStat, run, run_z);
     }
     if (AR && lane == 0) {  // the last CTA to finish advances the buffers' epoch for the next call
       uint32_t* hdr = reinterpret_cast<uint32_t*>(p.ar_bufs[p.ar_rank]);
@@ -1042,7 +1173,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if constexpr (HEAD) {
-      if (lane < p.M) cta_stats[lane * kMaxGrid + cta] = make_float4(run.m, __int_as_float(run.a), run.s, 0.f);
+      if (lane < p.M) {
+        cta_stats[lane * kMaxGrid + cta] = make_float4(run.m, __int_as_float(run.a), run.s, 0.f);
+        if constexpr (HEAD == 2) cta_draws[lane * kMaxGrid + cta] = make_float4(run_z.z, __int_as_float(run_z.a), run_z.s, 0.f);
+      }
       named_bar_sync(kBarEnd, kConsumerThreads + 32);
     }
     return;
@@ -1186,6 +1320,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             p.row_max[m] = st.m;
             p.row_argmax[m] = static_cast<long long>(st.a) + p.vocab_offset;
             p.row_lse[m] = st.m + logf(st.s);
+          }
+          if constexpr (HEAD == 2) {
+            SampleArg sz{-INFINITY, INT_MAX, 0.f};
+            for (int c = lane; c < p.G; c += 32) {
+              const float4 f = __ldcg(cta_draws + m * kMaxGrid + c);
+              sz = sa_max(sz, SampleArg{f.x, __float_as_int(f.y), f.z});
+            }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) sz = sa_max(sz, sa_shfl_xor(sz, off));
+            if (lane == 0) {
+              p.row_sample[m] = static_cast<long long>(sz.a) + p.vocab_offset;
+              p.row_sample_score[m] = sz.z;
+              p.row_sample_logit[m] = sz.s;
+            }
           }
         }
       }
@@ -1334,7 +1482,7 @@ void pick_tiles(int N, int K, int sms, int* bn, int* ks, int* dp_grid) {
   }
 }
 
-template <int BN, int NT, int KS, bool HEAD, bool AR, bool SILU>
+template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU>
 int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
            unsigned flags, cudaStream_t stream) {
   using C = Geo<BN, NT, KS>;
@@ -1405,7 +1553,7 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   return QF_OK;
 }
 
-template <int BN, int KS, bool HEAD, bool AR, bool SILU>
+template <int BN, int KS, int HEAD, bool AR, bool SILU>
 int launch_nt(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
               unsigned flags, cudaStream_t st) {
   if (p.M <= 8) return launch<BN, 1, KS, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
@@ -1428,7 +1576,7 @@ const TileShape& tile_override() {
   return v;
 }
 
-template <bool HEAD, bool AR = false, bool SILU = false>
+template <int HEAD, bool AR = false, bool SILU = false>
 int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
                unsigned flags, cudaStream_t st) {
   int bn = tile_override().bn, ks = tile_override().ks, dp_grid = 0;
@@ -1508,7 +1656,7 @@ int qf_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
-  return launch_any<false>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  return launch_any<0>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
 int qf_w8a16_gemm_silu_mul(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,
@@ -1534,7 +1682,7 @@ int qf_w8a16_gemm_silu_mul(const void* x, int64_t ldx, const int8_t* w, int64_t 
   p.K = K;
   p.ws = static_cast<uint8_t*>(ws);
   p.silu_I = N / 2;
-  return launch_any<false, false, true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
+  return launch_any<0, false, true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
 }
 
 int qf_w8a16_gemm_allreduce(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,
@@ -1569,7 +1717,7 @@ int qf_w8a16_gemm_allreduce(const void* x, int64_t ldx, const int8_t* w, int64_t
   p.ar_rank = rank;
   p.ar_max_count = max_count;
   for (int r = 0; r < world; ++r) p.ar_bufs[r] = static_cast<uint8_t*>(bufs[r]);
-  return launch_any<false, true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
+  return launch_any<0, true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
 }
 
 int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* logits,
@@ -1600,7 +1748,53 @@ int qf_w8a16_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, cons
   p.row_max = row_max;
   p.row_argmax = reinterpret_cast<long long*>(row_argmax);
   p.row_lse = row_lse;
-  return launch_any<true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
+  p.inv_temp = 1.0f;
+  return launch_any<1>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
+}
+
+int qf_w8a16_head_sample(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
+                         void* logits, int64_t ldl, int M, int N, int K, int n_valid, int64_t vocab_offset,
+                         float inv_temperature, uint64_t seed, uint64_t offset, float* row_max,
+                         int64_t* row_argmax, float* row_lse, int64_t* row_sample, float* row_sample_score,
+                         float* row_sample_logit, void* ws, size_t ws_bytes, unsigned flags, void* stream) {
+  int rc = check_common(x, ldx, w, ldw, scale, M, N, K, ws, ws_bytes);
+  if (rc) return rc;
+  if (M == 0) return QF_OK;
+  if (N == 0 || K == 0) return fail(QF_ERR_SHAPE, "the head needs N >= 1 and K >= 1");
+  if (n_valid < 1 || n_valid > N) return fail(QF_ERR_SHAPE, "n_valid must be in [1, N]");
+  if (!row_max || !row_argmax || !row_lse || !row_sample || !row_sample_score || !row_sample_logit)
+    return fail(QF_ERR_INVALID, "null row statistics output");
+  if (!(inv_temperature > 0.f) || !std::isfinite(inv_temperature))
+    return fail(QF_ERR_INVALID, "inv_temperature must be finite and > 0");
+  if (vocab_offset < 0 || vocab_offset + N > (1LL << 32)) return fail(QF_ERR_SHAPE, "vocabulary beyond 2^32 columns");
+  if (logits && M > 1 && ldl < N) return fail(QF_ERR_STRIDE, "ldl < N");
+  int dev;
+  DeviceInfo* dinfo;
+  rc = device_info(&dev, &dinfo);
+  if (rc) return rc;
+  Params p = {};
+  p.scale = scale;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ws = static_cast<uint8_t*>(ws);
+  p.logits = static_cast<__nv_bfloat16*>(logits);
+  p.ldl = ldl;
+  p.out_vec = reinterpret_cast<uintptr_t>(logits) % 16 == 0 && (M == 1 || ldl % 8 == 0);
+  p.n_valid = n_valid;
+  p.vocab_offset = vocab_offset;
+  p.row_max = row_max;
+  p.row_argmax = reinterpret_cast<long long*>(row_argmax);
+  p.row_lse = row_lse;
+  p.inv_temp = inv_temperature;
+  p.seed_lo = static_cast<uint32_t>(seed);
+  p.seed_hi = static_cast<uint32_t>(seed >> 32);
+  p.off_lo = static_cast<uint32_t>(offset);
+  p.off_hi = static_cast<uint32_t>(offset >> 32);
+  p.row_sample = reinterpret_cast<long long*>(row_sample);
+  p.row_sample_score = row_sample_score;
+  p.row_sample_logit = row_sample_logit;
+  return launch_any<2>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
 }
 
 int qf_workspace_status(void* ws, void* stream, int* status) {
@@ -1726,5 +1920,5 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
     e = cudaGetLastError();
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
-  return launch_any<false>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  return launch_any<0>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }

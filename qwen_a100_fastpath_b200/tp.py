@@ -163,3 +163,31 @@ def gather_head_stats(row_max, row_argmax, row_lse, group=None, out: torch.Tenso
         dist.all_gather(parts, local, group=group)
         out = torch.stack(parts)
     return combine_head_stats(out)
+
+
+def combine_head_samples(gathered: torch.Tensor):
+    """Fold per-shard ``[world, M, 3]`` (sample score, global sample column, sample logit) of
+    ``w8a16_head_sample`` into the draw of the full vocabulary: the shard with the largest score wins (lowest
+    global column on ties) -- the Gumbel-max draw of the unsharded head, since every shard's noise is keyed by the
+    global column.  Returns (sample int64, sample_logit fp32); its draft probability is
+    ``exp(sample_logit - lse)`` with the lse from ``combine_head_stats``."""
+    best = gathered[:, :, 0].max(dim=0).values
+    cand = torch.where(gathered[:, :, 0] == best, gathered[:, :, 1], torch.full_like(gathered[:, :, 1], float("inf")))
+    col = cand.min(dim=0).values
+    pick = (gathered[:, :, 1] == col) & (gathered[:, :, 0] == best)
+    logit = torch.where(pick, gathered[:, :, 2], torch.zeros_like(gathered[:, :, 2])).sum(dim=0)
+    return col.to(torch.int64), logit.float()
+
+
+def gather_head_samples(sample, sample_score, sample_logit, group=None):
+    """All-gather every rank's draw and combine them (same result on every rank)."""
+    world = dist.get_world_size(group)
+    local = torch.stack([sample_score.double(), sample.double(), sample_logit.double()], dim=1)
+    out = torch.empty((world, *local.shape), dtype=local.dtype, device=local.device)
+    if local.is_cuda:
+        dist.all_gather_into_tensor(out, local, group=group)
+    else:  # gloo: list form
+        parts = list(out.unbind(0))
+        dist.all_gather(parts, local, group=group)
+        out = torch.stack(parts)
+    return combine_head_samples(out)

@@ -264,3 +264,53 @@ def w8a16_head(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, n_vali
                            ws.data_ptr(), ws.numel(), flags, stream.cuda_stream)
     check("qf_w8a16_head", rc)
     return logits, row_max, row_arg, row_lse
+
+
+def w8a16_head_sample(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, temperature: float, seed: int,
+                      offset: int = 0, n_valid: int | None = None, vocab_offset: int = 0, want_logits: bool = True,
+                      pdl: bool | None = None):
+    """Int8 draft head with one temperature draw per row, for probabilistic drafting (the reference's draft head
+    is greedy only, plugin/qwen_fastpath/patches.py:176-185).  The logits are those of ``w8a16_head``; the
+    statistics are of the scaled logits ``s = logits / temperature``; each row also gets a Gumbel-max draw from
+    ``softmax(s)`` whose noise is Philox4x32-10 of ``(seed, offset, global column, row)`` (see
+    ``qf_w8a16_head_sample`` in ``include/qf_b200.h``), fused into the same pass over the logits.
+
+    Returns ``(logits, row_max, row_argmax, row_lse, sample, sample_score, sample_logit)``; the draft probability
+    of ``sample`` is ``exp(sample_logit - row_lse)``.  Vocab shards combine with ``tp.combine_head_samples``.
+    """
+    if not (temperature > 0.0) or temperature != temperature:
+        raise ValueError("temperature must be > 0 (use w8a16_head for greedy drafting)")
+    if x.dim() != 2:
+        raise ValueError("hidden states must be 2-D [M, K]")
+    M, K = x.shape
+    N = w_t.shape[1]
+    if w_t.shape[0] != K or M > SMALL_M or M < 1:
+        raise ValueError("bad head shapes")
+    if not (x.is_cuda and w_t.is_cuda and w_scale.is_cuda) or x.dtype != torch.bfloat16:
+        raise ValueError("head needs CUDA tensors and bf16 hidden states")
+    n_valid = N if n_valid is None else int(n_valid)
+    scale = w_scale.reshape(-1).contiguous()
+    if scale.numel() != N or scale.dtype != torch.float32:
+        raise ValueError("w_scale must hold N fp32 scales")
+    ldw = _check_weight(w_t, K)
+    x = _aligned_rows(x)
+    dev = x.device
+    logits = torch.empty((M, N), dtype=torch.bfloat16, device=dev) if want_logits else None
+    row_max = torch.empty((M,), dtype=torch.float32, device=dev)
+    row_arg = torch.empty((M,), dtype=torch.int64, device=dev)
+    row_lse = torch.empty((M,), dtype=torch.float32, device=dev)
+    sample = torch.empty((M,), dtype=torch.int64, device=dev)
+    score = torch.empty((M,), dtype=torch.float32, device=dev)
+    slogit = torch.empty((M,), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ws = workspace(dev, stream, LIB.qf_w8a16_workspace_bytes(M, N, K))
+    flags = _lib.QF_FLAG_PDL if (_PDL_DEFAULT if pdl is None else pdl) else 0
+    rc = LIB.qf_w8a16_head_sample(x.data_ptr(), x.stride(0), w_t.data_ptr(), ldw, scale.data_ptr(),
+                                  logits.data_ptr() if logits is not None else None,
+                                  logits.stride(0) if logits is not None else N, M, N, K, n_valid,
+                                  int(vocab_offset), float(1.0 / temperature), int(seed) & (2**64 - 1),
+                                  int(offset) & (2**64 - 1), row_max.data_ptr(), row_arg.data_ptr(),
+                                  row_lse.data_ptr(), sample.data_ptr(), score.data_ptr(), slogit.data_ptr(),
+                                  ws.data_ptr(), ws.numel(), flags, stream.cuda_stream)
+    check("qf_w8a16_head_sample", rc)
+    return logits, row_max, row_arg, row_lse, sample, score, slogit

@@ -40,6 +40,15 @@ def main() -> int:
         assert np.array_equal(mx.cpu().numpy(), mx_own)
         assert np.array_equal(am.cpu().numpy(), am_own)
         np.testing.assert_allclose(lse.cpu().numpy(), lse_own, rtol=2e-6)
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_head_sample
+    for (V, H, M) in [(4100, 2048, 5), (3000, 8192, 13)]:  # the fused draw on the same schedules
+        x, W, s = orc.make_inputs(V + H + 7, M, V, H)
+        out = w8a16_head_sample(to_dev_bf16(x, dev), torch.from_numpy(W).to(dev).t(), torch.from_numpy(s).to(dev),
+                                temperature=0.7, seed=5, offset=9, n_valid=V - 3, vocab_offset=100)
+        torch.cuda.synchronize()
+        from tests.test_gpu_head import check_draw
+        lg = from_dev_bf16(out[0])
+        check_draw(lg, V - 3, 0.7, 5, 9, 100, [o.cpu() if o is not None else None for o in out])
     from qwen_a100_fastpath_b200.w8a16 import workspace_status
     assert workspace_status() == 0
     print("ok")

@@ -127,3 +127,75 @@ def test_device_quantizer_bit_exact(dev):
         q_ref, s_ref = orc.quantize_rows(wb)
         assert np.array_equal(q.cpu().numpy(), q_ref)
         assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
+# ---- fused temperature draw (qf_w8a16_head_sample) -----------------------------------------------------------------
+def head_sample(dev, x_bits, W, s, T, seed, offset, n_valid, vocab_offset):
+    import torch
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_head_sample
+    out = w8a16_head_sample(to_dev_bf16(x_bits, dev), torch.from_numpy(W).to(dev).t(), torch.from_numpy(s).to(dev),
+                            temperature=T, seed=seed, offset=offset, n_valid=n_valid, vocab_offset=vocab_offset)
+    torch.cuda.synchronize()
+    return [o if o is None else o.cpu() for o in out]
+
+
+def check_draw(lg, n_valid, T, seed, offset, vocab_offset, out):
+    """The kernel's statistics and draw against the oracle on the kernel's own bf16 logits: statistics of the
+    scaled logits exact (lse within 2e-6); the draw identical wherever the oracle's best perturbed score leads the
+    second by more than fp32 noise (1e-4), else within 1e-4 of the best; the draw's logit exactly s there."""
+    _, mx, am, lse, smp, score, slog = out
+    o_mx, o_am, o_lse, o_smp, o_score, o_slog, margin = orc.head_sample(lg, n_valid, np.float32(1.0 / T), seed,
+                                                                        offset, vocab_offset)
+    assert np.array_equal(mx.numpy(), o_mx)
+    assert np.array_equal(am.numpy(), o_am)
+    np.testing.assert_allclose(lse.numpy(), o_lse, rtol=2e-6)
+    smp = smp.numpy()
+    clear = margin > 1e-4
+    assert np.array_equal(smp[clear], o_smp[clear])
+    sv = (orc.bf16_to_f32(lg)[:, :n_valid] * np.float32(1.0 / T)).astype(np.float32)
+    cols = smp - vocab_offset
+    assert np.all((cols >= 0) & (cols < n_valid))
+    z = sv.astype(np.float64) + orc.gumbel_noise(lg.shape[0], np.arange(n_valid) + vocab_offset, seed, offset)
+    rows = np.arange(lg.shape[0])
+    assert np.all(z[rows, cols] >= o_score - 1e-4)
+    np.testing.assert_allclose(score.numpy(), z[rows, cols], atol=1e-4, rtol=0)
+    assert np.array_equal(slog.numpy(), sv[rows, cols])
+
+
+@pytest.mark.parametrize("V,H,M,pad,T,vocab_offset", [(151936, 5120, 4, 0, 0.8, 0), (4100, 2048, 16, 36, 1.3, 0),
+                                                       (1000, 512, 5, 8, 0.5, 3000), (130, 128, 9, 2, 2.0, 7),
+                                                       (18992, 1024, 12, 0, 1.0, 18992 * 3)])
+def test_head_draw_matches_oracle(dev, V, H, M, pad, T, vocab_offset):
+    x, W, s = orc.make_inputs(V + H + M + 1, M, V, H)
+    for seed, offset in ((1234, 0), (2**40 + 5, 2**33 + 17)):
+        out = head_sample(dev, x, W, s, T, seed, offset, V - pad, vocab_offset)
+        lg = from_dev_bf16(out[0])
+        assert np.mean(lg != orc.w8a16_mm(x, W, s, "bf16")) < 0.01
+        check_draw(lg, V - pad, T, seed, offset, vocab_offset, out)
+
+
+def test_head_draw_unit_temperature_statistics_equal_greedy_head(dev):
+    V, H, M = 8192, 1024, 6
+    x, W, s = orc.make_inputs(21, M, V, H)
+    g_logits, g_mx, g_am, g_lse = [o.cpu() for o in head(dev, x, W, s, V - 10, 40)]
+    out = head_sample(dev, x, W, s, 1.0, 5, 6, V - 10, 40)
+    assert np.array_equal(from_dev_bf16(out[0]), from_dev_bf16(g_logits))
+    assert np.array_equal(out[1].numpy(), g_mx.numpy()) and np.array_equal(out[2].numpy(), g_am.numpy())
+    assert np.array_equal(out[3].numpy(), g_lse.numpy())
+
+
+def test_head_draw_vocab_shards_equal_unsharded(dev):
+    """Two vocab shards (the tensor-parallel head) draw exactly what the unsharded head draws."""
+    import torch
+    from qwen_a100_fastpath_b200 import tp
+    V, H, M = 4096, 1024, 5
+    x, W, s = orc.make_inputs(33, M, V, H)
+    full = head_sample(dev, x, W, s, 0.9, 11, 3, V, 0)
+    parts = []
+    for r in range(2):
+        n0, n1 = r * V // 2, (r + 1) * V // 2
+        o = head_sample(dev, x, np.ascontiguousarray(W[n0:n1]), s[n0:n1].copy(), 0.9, 11, 3, n1 - n0, n0)
+        parts.append(torch.stack([o[5].double(), o[4].double(), o[6].double()], dim=1))
+    col, logit = tp.combine_head_samples(torch.stack(parts))
+    assert np.array_equal(col.numpy(), full[4].numpy())
+    assert np.array_equal(logit.numpy(), full[6].numpy())

@@ -140,3 +140,26 @@ def test_allreduce_empty_and_buffer_size():
 def test_quantizer_argument_validation(args, code):
     assert _lib.LIB.qf_quantize_rows_int8(*args) == code
     assert _lib.LIB.qf_quantize_rows_int8(FAKE, 64, 0, 64, FAKE, 64, FAKE, None) == 0   # V == 0: no-op
+
+
+def head_sample(**kw):
+    a = dict(x=FAKE, ldx=5120, w=FAKE, ldw=5120, scale=FAKE, logits=FAKE, ldl=151936, M=4, N=151936, K=5120,
+             n_valid=151936, vocab_offset=0, inv_temperature=1.0, seed=1, offset=0, row_max=FAKE, row_argmax=FAKE,
+             row_lse=FAKE, row_sample=FAKE, row_sample_score=FAKE, row_sample_logit=FAKE, ws=FAKE,
+             ws_bytes=1 << 30, flags=0, stream=None)
+    a.update(kw)
+    return _lib.LIB.qf_w8a16_head_sample(*a.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(inv_temperature=0.0), -1),
+    (dict(inv_temperature=-2.0), -1),
+    (dict(inv_temperature=float("inf")), -1),
+    (dict(inv_temperature=float("nan")), -1),
+    (dict(row_sample=None), -1),
+    (dict(row_sample_logit=None), -1),
+    (dict(n_valid=0), -2),
+    (dict(vocab_offset=(1 << 32) - 100), -2),  # global columns must fit the generator's 32-bit counter word
+])
+def test_head_sample_argument_validation(kw, code):
+    assert head_sample(**kw) == code

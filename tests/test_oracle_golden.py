@@ -159,3 +159,66 @@ def test_silu_mul_oracle_matches_torch_on_bf16():
     got = orc.silu_mul(y, 300)
     assert np.mean(got != ref) < 0.01          # exp implementations may differ by an ulp before the bf16 rounding
     assert np.all(np.abs(orc.bf16_to_f32(got) - orc.bf16_to_f32(ref)) <= np.spacing(np.abs(orc.bf16_to_f32(ref)).astype(np.float32)) * 2 ** 16 + 1e-30)
+
+
+# ---- fused temperature draw (probabilistic drafting) -------------------------------------------------------------
+PHILOX_KAT = [  # Philox4x32-10 known-answer vectors published with the generator: counter, key -> output
+    ((0x00000000, 0x00000000, 0x00000000, 0x00000000), (0x00000000, 0x00000000),
+     (0x6627e8d5, 0xe169c58d, 0xbc57ac4c, 0x9b00dbd8)),
+    ((0xffffffff, 0xffffffff, 0xffffffff, 0xffffffff), (0xffffffff, 0xffffffff),
+     (0x408f276d, 0x41c83b0e, 0xa20bc7c6, 0x6d5451fd)),
+    ((0x243f6a88, 0x85a308d3, 0x13198a2e, 0x03707344), (0xa4093822, 0x299f31d0),
+     (0xd16cfe09, 0x94fdcceb, 0x5001e420, 0x24126ea1)),
+]
+
+
+@pytest.mark.parametrize("ctr,key,out", PHILOX_KAT)
+def test_philox_known_answers(ctr, key, out):
+    got = orc.philox4x32_10(np.array(ctr, dtype=np.uint64), key)
+    assert tuple(int(v) for v in got) == out
+
+
+def test_gumbel_draw_follows_softmax():
+    """The draw's empirical distribution over 48000 (row, offset) pairs matches softmax(logits / T): chi-square
+    with 15 degrees of freedom below its 0.999 quantile (37.7); deterministic (fixed seeds)."""
+    V, T = 16, 0.7
+    logits = orc.f32_to_bf16((np.random.RandomState(0).standard_normal((1, V)) * 1.5).astype(np.float32))
+    rows = np.repeat(logits, 16, axis=0)
+    counts = np.zeros(V)
+    for off in range(3000):
+        counts += np.bincount(orc.head_sample(rows, V, 1 / T, 1234, off)[3], minlength=V)
+    s = (orc.bf16_to_f32(logits)[0] * np.float32(1 / T)).astype(np.float64)
+    p = np.exp(s - s.max())
+    p /= p.sum()
+    n = counts.sum()
+    chi2 = ((counts - n * p) ** 2 / (n * p)).sum()
+    assert chi2 < 37.7, chi2
+
+
+def test_gumbel_draw_shards_match_unsharded():
+    """Vocab shards draw exactly what the unsharded head draws (noise keyed by the global column)."""
+    rs = np.random.RandomState(3)
+    V, M = 1200, 5
+    logits = orc.f32_to_bf16((rs.standard_normal((M, V)) * 2).astype(np.float32))
+    full = orc.head_sample(logits, V - 16, 1.25, 99, 7, 0)
+    for world in (2, 3, 4):
+        parts = []
+        for r in range(world):
+            n0, n1 = r * V // world, (r + 1) * V // world
+            nv = max(0, min(n1, V - 16) - n0)
+            if nv == 0:
+                continue
+            _, _, _, smp, sc, lg, _ = orc.head_sample(logits[:, n0:n1], nv, 1.25, 99, 7, n0)
+            parts.append((sc, smp, lg))
+        col, lg = orc.combine_head_samples(parts)
+        assert np.array_equal(col, full[3])
+        np.testing.assert_allclose(lg, full[5], rtol=0)
+
+
+def test_draw_statistics_at_unit_temperature_are_the_greedy_ones():
+    rs = np.random.RandomState(4)
+    logits = orc.f32_to_bf16((rs.standard_normal((3, 500)) * 2).astype(np.float32))
+    mx, am, lse, *_ = orc.head_sample(logits, 480, 1.0, 1, 2, 0)
+    g_mx, g_am, g_lse = orc.head_stats(logits, 480, 0)
+    assert np.array_equal(mx, g_mx) and np.array_equal(am, g_am)
+    np.testing.assert_allclose(lse, g_lse, rtol=1e-12)

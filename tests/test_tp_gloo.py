@@ -1,5 +1,6 @@
-"""Tensor-parallel host logic on CPU ranks (gloo, world size 2): row-parallel partial sums and the vocab-sharded
-head's (max, argmax, lse) gather match the unsharded oracle, ties resolved to the lowest global index."""
+"""Tensor-parallel host logic on CPU ranks (gloo, world size 2): row-parallel partial sums, the vocab-sharded
+head's (max, argmax, lse) gather and its temperature draw match the unsharded oracle, ties resolved to the lowest
+global index."""
 from __future__ import annotations
 
 import os
@@ -48,6 +49,14 @@ def worker(rank: int, world: int, port: int, result_dir: str):
         assert np.array_equal(g_am.numpy(), f_am)
         np.testing.assert_allclose(g_lse.numpy(), f_lse, rtol=1e-6)
         assert int(g_am[1]) == 100
+        # vocab-sharded temperature draw: every shard draws with noise keyed by the global column; the gathered
+        # draw equals the unsharded one
+        _, _, _, smp, score, slog, _ = orc.head_sample(logits[:, n0:n1], n1 - n0, 1 / 0.8, 77, 5, n0)
+        g_smp, g_slog = tp.gather_head_samples(torch.from_numpy(smp), torch.from_numpy(score.astype(np.float32)),
+                                               torch.from_numpy(slog))
+        f = orc.head_sample(logits, V, 1 / 0.8, 77, 5, 0)
+        assert np.array_equal(g_smp.numpy(), f[3])
+        np.testing.assert_allclose(g_slog.numpy(), f[5], rtol=1e-6)
         open(os.path.join(result_dir, f"ok{rank}"), "w").write("ok")
     finally:
         dist.destroy_process_group()
@@ -69,3 +78,14 @@ def test_combine_rules():
     assert abs(float(lse[0]) - float(torch.logsumexp(torch.tensor([3.0, 2.5, 1.0], dtype=torch.float64), 0))) < 1e-6
     with pytest.raises(ValueError):
         tp.shard_range(10, 0, 4)
+
+
+def test_sample_combine_rules():
+    from qwen_a100_fastpath_b200 import tp
+    # per shard (score, global column, logit): the largest score wins, lowest column on ties
+    g = torch.tensor([[[1.5, 7.0, 0.2]], [[2.5, 130.0, -1.0]], [[2.5, 129.0, 0.7]]], dtype=torch.float64)
+    col, logit = tp.combine_head_samples(g)
+    assert int(col[0]) == 129 and abs(float(logit[0]) - 0.7) < 1e-7
+    parts = [(g[r, :, 0].numpy(), g[r, :, 1].numpy().astype(np.int64), g[r, :, 2].numpy()) for r in range(3)]
+    o_col, o_logit = orc.combine_head_samples(parts)
+    assert int(o_col[0]) == 129 and abs(float(o_logit[0]) - 0.7) < 1e-12
