@@ -10,13 +10,15 @@
 //
 // * Tiles of BN output channels (BN = 128, 64 or 32, picked per shape) and pipeline stages of BN x KS weight
 //   bytes (the per-shape choice uses KS = 32768 / BN: 32 KiB stages of 256, 512 or 1024 contiguous bytes of each
-//   weight row; 16 KiB stages exist for tuning).  One persistent CTA per SM.
-// * Data-parallel + stream-K schedule: with ntiles = q*G + r, every CTA owns q whole tiles ("DP") and an equal
-//   share of the r * kiters stages of the remaining r tiles ("SK").  Each CTA runs its SK share first: the SK
-//   tiles' partial sums are handed to a fixup warp that reduces them (fp32 partials in the workspace, summed in
-//   CTA order, so results are deterministic) while the consumer warps stream the DP tiles.  No split reduction
-//   sits at the end of the kernel, and no memset or cast launches are needed (the reference zero-fills an fp32
-//   buffer for atomics and casts afterwards, w8a16.py:78-79, :83).
+//   weight row; 16 KiB stages exist for tuning).  One persistent CTA per SM, or, for small GEMMs whose tile
+//   count lies between half and all of the SMs, one CTA per tile (pick_tiles).
+// * Data-parallel + stream-K schedule: with ntiles = q*G + r, every CTA owns q whole tiles ("DP") and a share of
+//   the r * kiters stages of the remaining r tiles ("SK").  Each CTA runs its SK share first: the SK tiles'
+//   partial sums are handed to the epilogue warp, which reduces them (fp32 partials in the workspace, summed in
+//   CTA order, so results are deterministic) while the consumer warps stream the DP tiles.  When every tile is
+//   split (q == 0) each tile's reducing CTA gets a longer share, so the other shares finish first.  No memset
+//   or cast launches are needed (the reference zero-fills an fp32 buffer for atomics and casts afterwards,
+//   w8a16.py:78-79, :83).
 // * One producer lane issues per stage B = KS/128 weight boxes [BN rows x 128 bytes] and 2B activation boxes
 //   [8*NT tokens x 64 bf16] (cp.async.bulk.tensor, 128-byte swizzle, no multicast) into a ring of up to 10
 //   stages guarded by mbarriers.  With programmatic dependent launch the weight boxes of the first stages are
@@ -29,8 +31,10 @@
 //   bf16 -> fp16 (pairs (k, k+2), (k+1, k+3)) and the weights with one lop3 per byte pair; if any activation
 //   of the warp's chunk is outside the fp16 range the warp uses the exact bf16 conversion for that stage.
 // * Epilogue: fp32 accumulator * scale, one rounding to bf16 (or fp32 export), optional bias as the reference's
-//   second bf16 rounding (`y + bias`).  The head additionally reduces each tile's bf16 logits to per-row
-//   (max, first argmax, sum exp); the last CTA to finish folds all tiles in a fixed order.
+//   second bf16 rounding (`y + bias`); a dedicated warp finishes each tile while the consumers stream the next,
+//   and the consumers finish a CTA's last tile together.  The head additionally reduces each tile's bf16 logits
+//   to per-row (max, first argmax, sum exp) -- and, in the drawing instance, a Gumbel-max draw -- and the last
+//   CTA to finish folds all CTAs' statistics in a fixed order.
 // * Every wait on an mbarrier is bounded (global timer); on expiry the CTA records QF_ERR_TIMEOUT in the
 //   workspace, stops waiting, and the producer drains its own TMA copies before the CTA exits.
 #include <cuda.h>
