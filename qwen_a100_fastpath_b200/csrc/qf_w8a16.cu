@@ -72,7 +72,7 @@ constexpr int kBarFree = 3;                 // epilogue warp -> consumers: sRed 
 constexpr int kBarEnd = 4;                  // consumers + epilogue warp at the end (head only)
 constexpr int kBarCoop = 5;                 // epilogue warp -> consumers: peers' partial sums staged for the last tile
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;  // 4 s
-constexpr uint64_t kPeerWaitNs = 100000ull;        // stream-K reducer: wait for the other CTAs' partials (100 us)
+constexpr uint32_t kPeerWaitNs = 100000u;          // stream-K reducer: wait for the other CTAs' partials (100 us)
 constexpr int kSkSkewStages = 3;                   // default stream-K share skew (stages) when every tile is split
 
 // workspace layout (bytes); the prefix [0, kWsZeroBytes) must be zero before the first call
@@ -131,6 +131,7 @@ struct Params {
   int Tsk;     // r * kiters stream-K stages, split over the first Gsk CTAs
   int Gsk;
   int sk_skew; // q == 0: extra stages of each tile's reducing CTA over the other shares (0: even shares)
+  uint32_t peer_wait_ns;  // how long a stream-K reducer waits for the other shares' partial sums
   uint8_t* ws;
   int f16_path;
   uint32_t x_tx;  // activation bytes per stage: 2 B boxes of M rows x 128 bytes
@@ -998,7 +999,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Stream-K tiles: a CTA that holds a later part of a tile (its first tile) stores its partial sums and counts
     // itself in; the CTA holding the tile's first k-stages (its last stream-K tile, always the last to finish
     // it) is the tile's reducer: it waits for the others' count, prefetches their sums while its own stages still
-    // stream, and finishes the tile.  If that wait exceeds kPeerWaitNs (CTAs not co-resident), the reducer hands
+    // stream, and finishes the tile.  If that wait exceeds p.peer_wait_ns (CTAs not co-resident), the reducer hands
     // off like the others and the last one to count itself in reduces every slot.
     pdl_wait();
     const int g = lane >> 2;
@@ -1064,7 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool red_ok = false;
       if (is_red) {
         int ok = 0;
-        if (lane == 0) {
+        if (lane == 0 && p.peer_wait_ns > 0) {  // 0: hand off at once
           const int want = c_last - c_first;
           const uint64_t t0 = global_timer_ns();
           while (true) {
@@ -1072,7 +1073,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = 1;
               break;
             }
-            if (global_timer_ns() - t0 > kPeerWaitNs) break;
+            if (global_timer_ns() - t0 > p.peer_wait_ns) break;
             sleep_ns(128);
           }
         }
@@ -1413,6 +1414,17 @@ int grid_cap() {
   return cap;
 }
 
+// Stream-K reducer wait in ns (environment QF_PEER_WAIT_NS, read once; default kPeerWaitNs).  0 means no wait at
+// all: the tests set it so that every reducer hands off and the last-arriving share reduces the tile
+// (split_reduce_all), the path that otherwise runs only when the CTAs of a launch are not all resident.
+uint32_t peer_wait_ns() {
+  static const uint32_t v = [] {
+    const char* e = std::getenv("QF_PEER_WAIT_NS");
+    return e ? static_cast<uint32_t>(std::strtoul(e, nullptr, 10)) : kPeerWaitNs;
+  }();
+  return v;
+}
+
 // Stream-K share skew in stages (environment QF_SK_SKEW, read once; default kSkSkewStages): how many stages
 // longer the reducing CTA's share of a split tile is than the other shares, when every tile is split.
 int sk_skew_stages() {
@@ -1534,6 +1546,7 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   if (gsk > static_cast<long long>(kMaxSplit) * p.r) gsk = static_cast<long long>(kMaxSplit) * p.r;
   p.Gsk = static_cast<int>(gsk);
   if (p.q == 0) p.G = p.Gsk;  // all work is stream-K: CTAs without a share are not launched
+  p.peer_wait_ns = peer_wait_ns();
   p.sk_skew = 0;
   if (p.q == 0 && p.Gsk > p.r && static_cast<long long>(p.Gsk) * p.Tsk < (1LL << 31)) {
     // every tile split: uneven shares, the short ones keeping at least two stages

@@ -1,6 +1,7 @@
 """Work schedules and kernel instances the default choice does not reach: the grid capped to 1, 5 and 37 CTAs
-(environment QF_GRID_CAP), every tile shape BN:KS forced (environment QF_TILES), and even or differently skewed
-stream-K shares where every tile is split (environment QF_SK_SKEW).  All are read once per process, so each
+(environment QF_GRID_CAP), every tile shape BN:KS forced (environment QF_TILES), even or differently skewed
+stream-K shares where every tile is split (environment QF_SK_SKEW), and stream-K reducers that do not wait for the
+other shares (QF_PEER_WAIT_NS=0), so that the last share to finish reduces the tile.  All are read once per process, so each
 setting runs in a child process that checks GEMM and head results against the oracle."""
 from __future__ import annotations
 
@@ -14,16 +15,18 @@ import pytest
 pytestmark = pytest.mark.gpu
 REPO = Path(__file__).resolve().parent.parent
 
-SETTINGS = [("1", "", ""), ("5", "", ""), ("37", "", ""),
-            ("", "128:128", ""), ("", "128:256", ""), ("", "64:256", ""), ("", "64:512", ""), ("", "32:512", ""),
-            ("", "32:1024", ""), ("5", "128:256", ""), ("37", "32:1024", ""),
-            ("", "", "0"), ("", "", "1"), ("", "", "7"), ("100", "64:512", "5")]
+SETTINGS = [("1", "", "", ""), ("5", "", "", ""), ("37", "", "", ""),
+            ("", "128:128", "", ""), ("", "128:256", "", ""), ("", "64:256", "", ""), ("", "64:512", "", ""),
+            ("", "32:512", "", ""), ("", "32:1024", "", ""), ("5", "128:256", "", ""), ("37", "32:1024", "", ""),
+            ("", "", "0", ""), ("", "", "1", ""), ("", "", "7", ""), ("100", "64:512", "5", ""),
+            # reducers hand off at once: the last-arriving share reduces the tile (the not-co-resident path)
+            ("", "", "", "0"), ("37", "", "", "0"), ("", "32:1024", "0", "0"), ("5", "128:256", "", "0")]
 
 
-@pytest.mark.parametrize("cap,tiles,skew", SETTINGS, ids=lambda v: v or "-")
-def test_schedules_and_tile_shapes_match_oracle(dev, cap, tiles, skew):
+@pytest.mark.parametrize("cap,tiles,skew,peer", SETTINGS, ids=lambda v: v or "-")
+def test_schedules_and_tile_shapes_match_oracle(dev, cap, tiles, skew, peer):
     env = dict(os.environ)
-    for k in ("QF_GRID_CAP", "QF_TILES", "QF_SK_SKEW"):
+    for k in ("QF_GRID_CAP", "QF_TILES", "QF_SK_SKEW", "QF_PEER_WAIT_NS"):
         env.pop(k, None)
     if cap:
         env["QF_GRID_CAP"] = cap
@@ -31,6 +34,8 @@ def test_schedules_and_tile_shapes_match_oracle(dev, cap, tiles, skew):
         env["QF_TILES"] = tiles
     if skew:
         env["QF_SK_SKEW"] = skew
+    if peer:
+        env["QF_PEER_WAIT_NS"] = peer
     r = subprocess.run([sys.executable, "-m", "tests._grid_cap_case"], cwd=REPO, env=env, capture_output=True,
                        text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
