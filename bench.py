@@ -67,7 +67,7 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
     ap.add_argument("--sweep-out", default="")
-    ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head: a few "
+    ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head,lm_head_sample: a few "
                     "launches of each at --m (the small case for an ncu capture), then exit")
     return ap.parse_args()
 
@@ -565,10 +565,11 @@ def run_sweep(args, local: int):
 def run_profile_gemm(args, local: int):
     """Two launches of each named GEMM (int8 weights U[-127,127], distinct per launch) at M = --m."""
     import torch
-    from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_mm
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_head_sample, w8a16_mm
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     shapes = {nm: (N, K) for nm, N, K, _ in LAYER + [HEAD]}
+    shapes["lm_head_sample"] = shapes["lm_head"]
     g = torch.Generator(device=dev).manual_seed(3)
     for name in args.profile_gemm.split(","):
         N, K = shapes[name]
@@ -579,6 +580,8 @@ def run_profile_gemm(args, local: int):
             torch.cuda.synchronize()
             if name == "lm_head":
                 w8a16_head(x, W.t(), s)
+            elif name == "lm_head_sample":
+                w8a16_head_sample(x, W.t(), s, temperature=0.8, seed=1, offset=0)
             else:
                 w8a16_mm(x, W.t(), s, None, torch.bfloat16)
             torch.cuda.synchronize()
