@@ -67,6 +67,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
     ap.add_argument("--sweep-out", default="")
+    ap.add_argument("--host-overhead", action="store_true", help="eager host time per call of the public entry "
+                    "points (enqueue only) against the kernel's device time, o_proj at --m")
     ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head,lm_head_sample: a few "
                     "launches of each at --m (the small case for an ncu capture), then exit")
     return ap.parse_args()
@@ -310,7 +312,8 @@ def max_over_ranks(v: float) -> float:
 
 
 def traffic_from_profiles():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if present."""
+    """DRAM bytes per launch of the dominant kernel, read from the committed ncu summary of the M = 5 step (not
+    measured by this run: ncu cannot run inside a timed bench).  Returns (bytes, source file)."""
     p = REPO / "profiles" / "w8a16_gemm_step_m5_ncu.md"
     if not p.exists():
         return None, None
@@ -420,7 +423,9 @@ def run_ours(args, rank: int, world: int, local: int):
                     "kernel": "w8a16_kernel<BN, NT=1> (qkv/o_proj/gate_up/down launches of the step)",
                     "bytes_per_launch": round(gemm_bytes), "us_per_launch": round(per_launch_ms * 1e3, 3),
                     "peak_source": peak_src + ", 'of measured'", "frac_of_nominal_8TBs": round(achieved / NOMINAL_HBM_GBS, 4),
-                    "traffic_source": tsrc,
+                    "traffic_source": (f"profiles/{tsrc}: ncu dram__bytes_read.sum + dram__bytes_write.sum per "
+                                       "launch of the decoder GEMMs of a committed M=5 step capture, not measured "
+                                       "by this run" if tsrc else None),
                     "timing": ("decoder-GEMM phase of the step graph (PDL on) between CUDA events at the step start "
                                "and after the last GEMM, / 256 launches, median over replays" if phase else
                                "CUDA events around every launch of a replay of the same step (PDL off), median of 5"),
@@ -589,6 +594,57 @@ def run_profile_gemm(args, local: int):
     print("profile-gemm done:", args.profile_gemm)
 
 
+def run_host_overhead(args, local: int):
+    """Host cost of one eager call (argument checks, ctypes, tensor-map encoding, launch) of the C-ABI entry point,
+    of ``w8a16_mm`` and of the ``qf_int8_linear`` op body, against the device time of the same launch, for o_proj at
+    M = --m.  The host loop enqueues only (no synchronisation inside the timed loop)."""
+    import torch
+    from qwen_a100_fastpath_b200 import _lib
+    from qwen_a100_fastpath_b200.patches import make_int8_linear_op
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_mm, workspace
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N, K, M = 5120, 8192, args.m
+    g = torch.Generator(device=dev).manual_seed(5)
+    W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+    s = torch.rand(N, device=dev, generator=g) * 0.009 + 0.001
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    op, _ = make_int8_linear_op()
+    stream = torch.cuda.current_stream(dev)
+    ws = workspace(dev, stream, _lib.LIB.qf_w8a16_workspace_bytes(M, N, K))
+
+    def c_abi():
+        _lib.LIB.qf_w8a16_gemm(x.data_ptr(), K, W.data_ptr(), K, s.data_ptr(), None, y.data_ptr(), N,
+                               _lib.QF_DTYPE_BF16, M, N, K, ws.data_ptr(), ws.numel(), 0, stream.cuda_stream)
+
+    calls = {"c_abi_ctypes": c_abi,
+             "w8a16_mm": lambda: w8a16_mm(x, W.t(), s, None, torch.bfloat16, out=y, pdl=False),
+             "qf_int8_linear_op": lambda: op(x, W.t(), s.view(N, 1), None)}
+    res = {}
+    n = 2000
+    for name, fn in calls.items():
+        for _ in range(50):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        host_us = (time.perf_counter() - t0) / n * 1e6
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(200):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = {"host_us_per_call": round(host_us, 2), "device_us_per_call": round(e0.elapsed_time(e1) * 5, 2)}
+    print(json.dumps({"host_overhead": res, "gemm": f"o_proj {N}x{K}", "m": M,
+                      "note": "host_us: enqueue cost per eager call (no sync in the loop); device_us: back-to-back "
+                              "launches on one weight (L2-resident, so shorter than the HBM-bound step)"}),
+          flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -606,6 +662,10 @@ def main():
     if args.profile_gemm:
         if rank == 0:
             run_profile_gemm(args, local)
+        return
+    if args.host_overhead:
+        if rank == 0:
+            run_host_overhead(args, local)
         return
     run_ours(args, rank, world, local)
 

@@ -109,16 +109,24 @@ int qf_w8a16_head_sample(const void* x, int64_t ldx, const int8_t* w, int64_t ld
  * must not call cudaMalloc, which can synchronise the device.  Same arguments and math as qf_w8a16_gemm
  * without ws / ws_bytes.  Its scratch (split-tile counters and fp32 partial tiles) is a fixed
  * QF_NOALLOC_SCRATCH_BYTES array inside the library, held by every GPU that loads the library until the
- * process exits; N is limited to QF_NOALLOC_MAX_N (larger N returns QF_ERR_SHAPE).  The first call on a device
- * looks up that array's device address (cudaGetSymbolAddress) and must be made with the device current,
- * before any stream capture.  Every call clears the scratch's counters with one cudaMemsetAsync on `stream`.
- * All calls share the one array, so calls whose kernels overlap on the GPU (different streams) race: order
- * them on one stream. */
-#define QF_NOALLOC_MAX_N 65536
+ * process exits.  N is limited to QF_NOALLOC_MAX_N because the array holds 8192 tile counters and a tile is at
+ * least 32 output channels high (larger N returns QF_ERR_SHAPE), and the device may have at most 160 SMs (two
+ * partial-tile slots per CTA).  The first call on a device (or the first qf_w8a16_noalloc_status) looks up that
+ * array's device address (cudaGetSymbolAddress) and enqueues one zero fill of its counters on `stream`; it must
+ * be made with the device current, before any stream capture.  Later calls enqueue only the kernel: each call
+ * leaves the counters at zero for the next.  All calls share the one array, so calls whose kernels overlap on the
+ * GPU (different streams) race: order them on one stream.  A device-side timeout is kept in the array until
+ * qf_w8a16_noalloc_status reads it. */
+#define QF_NOALLOC_MAX_N 262144
 #define QF_NOALLOC_SCRATCH_BYTES 2655232u
 int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
                           const void* bias, void* y, int64_t ldy, int y_dtype, int M, int N, int K,
                           unsigned flags, void* stream);
+/* Reads and clears the sticky device error flag of the allocation-free entry point's fixed scratch on the current
+ * device (synchronises `stream`); *status receives QF_OK or QF_ERR_TIMEOUT.  After a timeout it also zeroes the
+ * scratch's tile counters, so the next call starts clean.  No counterpart in the reference.  Not for the hot
+ * path. */
+int qf_w8a16_noalloc_status(void* stream, int* status);
 
 /* gate_up projection with the MLP activation fused into its epilogue: w holds the merged [gate; up] weight (rows
  * [0, N/2) gate, [N/2, N) up, vLLM's MergedColumnParallelLinear), and the result is the activation

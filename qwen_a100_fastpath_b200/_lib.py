@@ -17,7 +17,7 @@ QF_DTYPE_F32 = 1
 QF_MAX_M = 16
 QF_MAX_N = 1048576
 QF_FLAG_PDL = 1
-QF_NOALLOC_MAX_N = 65536
+QF_NOALLOC_MAX_N = 262144
 QF_AR_MAX_RANKS = 8
 QF_AR_MAX_CHUNKS = 256
 QF_IPC_HANDLE_BYTES = 64
@@ -42,6 +42,7 @@ SIGNATURES = [
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64,
       _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_uint, _c.c_void_p]),
     ("qf_workspace_status", _c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(_c.c_int)]),
+    ("qf_w8a16_noalloc_status", _c.c_int, [_c.c_void_p, _c.POINTER(_c.c_int)]),
     ("qf_w8a16_gemm_silu_mul", _c.c_int,
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int, _c.c_int,
       _c.c_int, _c.c_void_p, _c.c_size_t, _c.c_uint, _c.c_void_p]),

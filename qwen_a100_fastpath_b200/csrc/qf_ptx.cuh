@@ -156,7 +156,9 @@ __device__ __forceinline__ void dequant_i8x4_f16(uint32_t w, uint32_t& a02, uint
 
 // Two bf16x2 words (x0, x1), (x2, x3) -> f16x2 (x0, x2), (x1, x3), the activation pairing of
 // dequant_i8x4_f16.  Returns non-zero if any value is outside the fp16 range (|x| >= 65536, Inf, NaN):
-// the magnitude bits plus 0x3880 reach bit 15 exactly when they are >= 0x4780 (bf16 65536).
+// the magnitude bits plus 0x3880 reach bit 15 exactly when they are >= 0x4780 (bf16 65536).  Values below
+// fp16's normal range (|x| < 2^-14) become fp16 subnormals, which keep 2^-24 absolute resolution: not exact
+// there, but within 2^-25 of the bf16 value.
 __device__ __forceinline__ uint32_t bf16x4_to_f16_pairs(uint32_t w0, uint32_t w1, uint32_t& o0, uint32_t& o1) {
   const float x0 = __uint_as_float(w0 << 16), x1 = __uint_as_float(w0 & 0xFFFF0000u);
   const float x2 = __uint_as_float(w1 << 16), x3 = __uint_as_float(w1 & 0xFFFF0000u);

@@ -27,9 +27,12 @@
 //   box's 16-byte k chunks; lane (g, t) takes chunk c = (t ^ h) | ((t & 1) << 2), which keeps both the swizzled
 //   weight reads and the activation reads free of bank conflicts.  Weights are converted to exact 16-bit floats in
 //   registers and fed to mma.sync m16n8k16 as the 16-row A operand ("swap AB"); the M <= 16 tokens are the
-//   8-column B operand (NT = 1 or 2 token tiles).  fp16 path: each warp converts its activation fragments
-//   bf16 -> fp16 (pairs (k, k+2), (k+1, k+3)) and the weights with one lop3 per byte pair; if any activation
-//   of the warp's chunk is outside the fp16 range the warp uses the exact bf16 conversion for that stage.
+//   8-column B operand (NT = 1 or 2 token tiles).  fp16 path (default): each warp converts its activation
+//   fragments bf16 -> fp16 (pairs (k, k+2), (k+1, k+3)) and the weights with one lop3 per byte pair; if any
+//   activation of the warp's chunk is outside the fp16 range the warp uses the bf16 path for that stage.  The
+//   weight conversion is exact in both paths; the fp16 activation is exact except below fp16's normal range
+//   (|x| < 2^-14), where it rounds to an fp16 subnormal (absolute error <= 2^-25 per activation, far below the
+//   fp32 accumulation noise).  QF_F16_PATH=0 (under QF_TEST_OVERRIDES=1) keeps every product exact.
 // * Epilogue: fp32 accumulator * scale, one rounding to bf16 (or fp32 export), optional bias as the reference's
 //   second bf16 rounding (`y + bias`); a dedicated warp finishes each tile while the consumers stream the next,
 //   and the consumers finish a CTA's last tile together.  The head additionally reduces each tile's bf16 logits
@@ -760,20 +763,43 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
   }
 }
 
+// Scale and bias of the rows 16 w + g and 16 w + g + 8 of `tile` for consumer lane (w, g): what coop_finish_tile
+// needs, loaded when the consumers start so that their memory latency stays off the launch's critical path.
+struct RowScale {
+  float s0, s1, b0, b1;
+};
+template <int BN>
+__device__ __forceinline__ RowScale load_row_scale(const Params& p, int tile, int warp, int g) {
+  RowScale r{0.f, 0.f, 0.f, 0.f};
+  if (tile < 0 || 16 * warp >= BN) return r;
+  const int n0 = tile * BN + 16 * warp + g;
+  const int n1 = n0 + 8;
+  if (n0 < p.N) r.s0 = __ldg(p.scale + n0);
+  if (n1 < p.N) r.s1 = __ldg(p.scale + n1);
+  if (p.bias) {
+    if (n0 < p.N) r.b0 = __bfloat162float(p.bias[n0]);
+    if (n1 < p.N) r.b1 = __bfloat162float(p.bias[n1]);
+  }
+  return r;
+}
+
 // The CTA's last tile, finished by the eight consumer warps together instead of the epilogue warp alone (nothing is
-// left to overlap with it, so it sits on the launch's critical path): warp w sums m-tiles w, w + 8, ... from the
-// warps' partial sums in sRed -- starting from the stream-K peers' sums in sPeer when `peers` -- in the epilogue
-// warp's order, so the bits are the same as finish_tile's, then all consumers store the staged rows.
-// Plain GEMM instances with bf16 output only.
+// left to overlap with it, so it sits on the launch's critical path): warp w sums m-tile w from the warps' partial
+// sums in sRed -- starting from the stream-K peers' sums in sPeer when `peers` -- in the epilogue warp's order, so the
+// bits are the same as finish_tile's, then all consumers store the staged rows.  `rs` holds the m-tile's scales and
+// bias (load_row_scale).  Plain GEMM instances with bf16 output only.
 template <int BN, int NT, int MW, int NMW>
 __device__ __forceinline__ void coop_finish_tile(const Params& p, int tile, int warp, const float* sRed,
-                                                 const float* sPeer, bool peers, __nv_bfloat16* sOut) {
+                                                 const float* sPeer, bool peers, __nv_bfloat16* sOut,
+                                                 const RowScale& rs) {
   constexpr int MT = BN / 16;
   constexpr int OS = BN + 8;
+  static_assert(MT <= kConsumerWarps, "one m-tile per consumer warp");
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2;
   const int t = lane & 3;
-  for (int mt = warp; mt < MT; mt += kConsumerWarps) {
+  if (warp < MT) {
+    const int mt = warp;
     float v[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -790,25 +816,16 @@ __device__ __forceinline__ void coop_finish_tile(const Params& p, int tile, int 
 #pragma unroll
           for (int e = 0; e < 4; ++e) v[nt][e] += o[nt * 4 + e];
       }
-    const int n0 = tile * BN + 16 * mt + g;
-    const int n1 = n0 + 8;
-    const float s0 = n0 < p.N ? __ldg(p.scale + n0) : 0.f;
-    const float s1 = n1 < p.N ? __ldg(p.scale + n1) : 0.f;
-    float b0 = 0.f, b1 = 0.f;
-    if (p.bias) {
-      if (n0 < p.N) b0 = __bfloat162float(p.bias[n0]);
-      if (n1 < p.N) b1 = __bfloat162float(p.bias[n1]);
-    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int bq = 0; bq < 2; ++bq) {
         const int m = 8 * nt + 2 * t + bq;
-        __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][bq] * s0);
-        __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + bq] * s1);
+        __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][bq] * rs.s0);
+        __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + bq] * rs.s1);
         if (p.bias) {
-          r0 = __float2bfloat16_rn(__bfloat162float(r0) + b0);
-          r1 = __float2bfloat16_rn(__bfloat162float(r1) + b1);
+          r0 = __float2bfloat16_rn(__bfloat162float(r0) + rs.b0);
+          r1 = __float2bfloat16_rn(__bfloat162float(r1) + rs.b1);
         }
         sOut[m * OS + 16 * mt + g] = r0;
         sOut[m * OS + 16 * mt + g + 8] = r1;
@@ -1207,6 +1224,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ctid = threadIdx.x;  // 0..255 among consumers
   const bool use_f16 = p.f16_path != 0;
   int tcount = 0;
+  // scales and bias of the CTA's last tile (its last whole tile, else the last tile of its stream-K share), which the
+  // consumers may finish themselves
+  RowScale last_rs{0.f, 0.f, 0.f, 0.f};
+  if constexpr (kCoopLast) {
+    if (!p.y_f32 && n_iter > 0)
+      last_rs = load_row_scale<BN>(p, p.q > 0 ? p.r + cta + (p.q - 1) * p.G : (it.sk_end - 1) / p.kiters, warp, g);
+  }
 
   float acc[MW][NT][4];
 #pragma unroll
@@ -1290,7 +1314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (mode == 2) named_bar_sync(kBarCoop, kConsumerThreads + 32);
       if (mode != 0)
         coop_finish_tile<BN, NT, MW, NMW>(p, cur_tile, warp, sRed, reinterpret_cast<const float*>(sW), mode == 2,
-                                          sOut);
+                                          sOut, last_rs);
     } else {
       named_bar_arrive(kBarReady, kConsumerThreads + 32);
     }
@@ -1405,41 +1429,52 @@ int device_info(int* dev_out, DeviceInfo** info_out) {
   return QF_OK;
 }
 
-// Optional upper bound on the grid (environment QF_GRID_CAP, read once): lets tests exercise other schedules.
+// Test and tuning knobs (QF_GRID_CAP, QF_TILES, QF_SK_SKEW, QF_PEER_WAIT_NS, QF_F16_PATH) are read only when the
+// environment also sets QF_TEST_OVERRIDES=1, so that a stray variable in a deployment cannot change the schedule or
+// the arithmetic path.  Each is read once per process.
+const char* test_env(const char* name) {
+  static const bool on = [] {
+    const char* v = std::getenv("QF_TEST_OVERRIDES");
+    return v != nullptr && std::strcmp(v, "1") == 0;
+  }();
+  return on ? std::getenv(name) : nullptr;
+}
+
+// Optional upper bound on the grid (QF_GRID_CAP): lets tests exercise other schedules.
 int grid_cap() {
   static const int cap = [] {
-    const char* v = std::getenv("QF_GRID_CAP");
+    const char* v = test_env("QF_GRID_CAP");
     return v ? std::atoi(v) : 0;
   }();
   return cap;
 }
 
-// Stream-K reducer wait in ns (environment QF_PEER_WAIT_NS, read once; default kPeerWaitNs).  0 means no wait at
+// Stream-K reducer wait in ns (QF_PEER_WAIT_NS; default kPeerWaitNs).  0 means no wait at
 // all: the tests set it so that every reducer hands off and the last-arriving share reduces the tile
 // (split_reduce_all), the path that otherwise runs only when the CTAs of a launch are not all resident.
 uint32_t peer_wait_ns() {
   static const uint32_t v = [] {
-    const char* e = std::getenv("QF_PEER_WAIT_NS");
+    const char* e = test_env("QF_PEER_WAIT_NS");
     return e ? static_cast<uint32_t>(std::strtoul(e, nullptr, 10)) : kPeerWaitNs;
   }();
   return v;
 }
 
-// Stream-K share skew in stages (environment QF_SK_SKEW, read once; default kSkSkewStages): how many stages
+// Stream-K share skew in stages (QF_SK_SKEW; default kSkSkewStages): how many stages
 // longer the reducing CTA's share of a split tile is than the other shares, when every tile is split.
 int sk_skew_stages() {
   static const int v = [] {
-    const char* e = std::getenv("QF_SK_SKEW");
+    const char* e = test_env("QF_SK_SKEW");
     return e ? std::atoi(e) : kSkSkewStages;
   }();
   return v;
 }
 
-// Activation path (environment QF_F16_PATH, read once): 1 (default) converts activations to fp16 for the cheaper
+// Activation path (QF_F16_PATH): 1 (default) converts activations to fp16 for the cheaper
 // exact weight conversion (warps fall back to bf16 where activations leave the fp16 range); 0 keeps bf16.
 int f16_path() {
   static const int v = [] {
-    const char* e = std::getenv("QF_F16_PATH");
+    const char* e = test_env("QF_F16_PATH");
     return e ? std::atoi(e) : 1;
   }();
   return v;
@@ -1577,7 +1612,7 @@ int launch_nt(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& 
   return launch<BN, 2, KS, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
-// Optional fixed tile shape (environment QF_TILES="BN:KS", read once; 0 = the per-shape choice): used by the
+// Optional fixed tile shape (QF_TILES="BN:KS"; 0 = the per-shape choice): used by the
 // tests to run every kernel instance, and for tuning.
 struct TileShape {
   int bn = 0, ks = 0;
@@ -1585,7 +1620,7 @@ struct TileShape {
 const TileShape& tile_override() {
   static const TileShape v = [] {
     TileShape t;
-    if (const char* e = std::getenv("QF_TILES")) {
+    if (const char* e = test_env("QF_TILES")) {
       if (std::sscanf(e, "%d:%d", &t.bn, &t.ks) != 2) t = TileShape{};
     }
     return t;
@@ -1861,6 +1896,8 @@ namespace {
 constexpr int kNoAllocMaxGrid = 160;                 // CTAs: partial-tile slots are 2 per CTA
 constexpr size_t kNoAllocBytes = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kNoAllocMaxGrid;
 static_assert(kNoAllocBytes == QF_NOALLOC_SCRATCH_BYTES, "header value out of date");
+// Tiles are at least 32 output channels high and the array holds kMaxTiles tile counters.
+static_assert(static_cast<long long>(QF_NOALLOC_MAX_N) <= 32LL * kMaxTiles, "tile counters of the fixed scratch");
 
 __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
@@ -1868,14 +1905,18 @@ std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {};
 
 // Device address of the scratch array for the current device, looked up once per device (with that device
-// current).  The host-side symbol is only a stand-in, never a device address.
-int noalloc_scratch(int dev, void** out) {
+// current).  The host-side symbol is only a stand-in, never a device address.  The first lookup also zeroes the
+// error word and the tile counters, enqueued on `stream` ahead of the first kernel; from then on every kernel
+// leaves its counters at zero again, as on a caller's workspace.
+int noalloc_scratch(int dev, cudaStream_t stream, void** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || !ptr)
       return fail(QF_ERR_LAUNCH, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    e = cudaMemsetAsync(ptr, 0, kWsZeroBytes, stream);
+    if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
     g_noalloc_ptr[dev] = ptr;
   }
   *out = g_noalloc_ptr[dev];
@@ -1891,8 +1932,8 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
   if (M < 0 || N < 0 || K < 0) return fail(QF_ERR_SHAPE, "negative size");
   if (M > QF_MAX_M) return fail(QF_ERR_SHAPE, "M > 16: the small-M path handles at most 16 rows");
   if (N > QF_NOALLOC_MAX_N)
-    return fail(QF_ERR_SHAPE, "N above QF_NOALLOC_MAX_N (65536): the fixed scratch of the allocation-free entry "
-                              "point holds tile counters for at most that many output channels");
+    return fail(QF_ERR_SHAPE, "N above QF_NOALLOC_MAX_N (262144): the fixed scratch of the allocation-free entry "
+                              "point holds 8192 tile counters, and tiles are at least 32 output channels high");
   if (M == 0 || N == 0) return QF_OK;
   if (!scale || !y) return fail(QF_ERR_INVALID, "null scale or y");
   if (y_dtype != QF_DTYPE_BF16 && y_dtype != QF_DTYPE_F32) return fail(QF_ERR_DTYPE, "y_dtype must be bf16 or fp32");
@@ -1912,14 +1953,13 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
   if (rc) return rc;
   if (dinfo->sm_count > kNoAllocMaxGrid)
     return fail(QF_ERR_SHAPE, "device has more SMs than the allocation-free scratch provides partial-tile slots for");
-  void* scratch = nullptr;
-  rc = noalloc_scratch(dev, &scratch);
-  if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The array keeps the previous call's contents: clear the header and the tile counters this call can use.
-  const size_t ntiles = (static_cast<size_t>(N) + 31) / 32;
-  cudaError_t e = cudaMemsetAsync(scratch, 0, kWsCounters + sizeof(int) * (ntiles < kMaxTiles ? ntiles : kMaxTiles), st);
-  if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  void* scratch = nullptr;
+  rc = noalloc_scratch(dev, st, &scratch);
+  if (rc) return rc;
+  // The array keeps the previous call's contents.  What must start at zero -- the tile counters -- was zeroed when
+  // the array was first used on this device, and every call leaves it at zero again; the error word stays set
+  // until qf_w8a16_noalloc_status reads it.
   Params p = {};
   p.scale = scale;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
@@ -1934,8 +1974,29 @@ extern "C" int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w
   if (K == 0) {
     const int64_t total = static_cast<int64_t>(M) * N;
     fill_empty_k_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(p);
-    e = cudaGetLastError();
+    const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
   }
   return launch_any<0>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+}
+
+extern "C" int qf_w8a16_noalloc_status(void* stream, int* status) {
+  if (!status) return fail(QF_ERR_INVALID, "null status");
+  int dev;
+  DeviceInfo* dinfo;
+  int rc = device_info(&dev, &dinfo);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* scratch = nullptr;
+  rc = noalloc_scratch(dev, st, &scratch);
+  if (rc) return rc;
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, scratch, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  // A call that gave up waiting may have left tile counters set: start the next call from a clean array.
+  if (e == cudaSuccess && v != 0) e = cudaMemsetAsync(scratch, 0, kWsZeroBytes, st);
+  if (e == cudaSuccess && v != 0) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
+  *status = v;
+  return QF_OK;
 }

@@ -28,6 +28,15 @@ logger = logging.getLogger("vllm.qwen_fastpath")
 # ----------------------------------------------------------------------------------------------
 # QWEN_FAST_LINEAR
 # ----------------------------------------------------------------------------------------------
+def w8a8_fallback(x2: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor, bias: torch.Tensor | None,
+                  out_dtype: torch.dtype) -> torch.Tensor:
+    """vLLM's stock W8A8 path for what the small-M kernel does not take (patches.py:99-100 of the reference):
+    dynamic per-token int8 activations and the CUTLASS int8 GEMM."""
+    from vllm import _custom_ops as ops
+    x_q, x_s, _ = ops.scaled_int8_quant(x2.contiguous(), None, None, symmetric=True)
+    return ops.cutlass_scaled_mm(x_q, w_q, scale_a=x_s, scale_b=w_s, out_dtype=out_dtype, bias=bias)
+
+
 def make_int8_linear_op():
     """The ``qf_int8_linear`` implementation and its fake (shape-only) counterpart."""
     from .w8a16 import SMALL_M, pick_config, w8a16_mm, weight_supported
@@ -44,10 +53,7 @@ def make_int8_linear_op():
             if cfg is not None:
                 y = w8a16_mm(x2, w_q, w_s, cfg, x.dtype, bias=bias, pdl=True)
                 return y.view(*lead, N)
-        from vllm import _custom_ops as ops
-        x_q, x_s, _ = ops.scaled_int8_quant(x2.contiguous(), None, None, symmetric=True)
-        y = ops.cutlass_scaled_mm(x_q, w_q, scale_a=x_s, scale_b=w_s, out_dtype=x.dtype, bias=bias)
-        return y.view(*lead, N)
+        return w8a8_fallback(x2, w_q, w_s, bias, x.dtype).view(*lead, N)
 
     def qf_int8_linear_fake(x: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor,
                             bias: torch.Tensor | None) -> torch.Tensor:
@@ -150,6 +156,31 @@ def int8_head(model, hidden_states: torch.Tensor, want_logits: bool = True):
     return out
 
 
+def draft_compute_logits(model, hidden_states: torch.Tensor, spec_step_idx, orig_logits):
+    """Body of the patched ``Qwen3_5MTP.compute_logits`` (patches.py:168-174 of the reference): the int8 head's
+    logits cut to ``org_vocab_size``, or the original method where the int8 head does not apply."""
+    out = int8_head(model, hidden_states)
+    if out is None:
+        return orig_logits(model, hidden_states, spec_step_idx)
+    return out[0][..., : model.logits_processor.org_vocab_size]
+
+
+def draft_get_top_tokens(model, hidden_states: torch.Tensor, orig_logits, orig_top=None):
+    """Body of the patched ``Qwen3_5MTP.get_top_tokens`` (patches.py:176-185 of the reference): the int8 head's
+    fused argmax (vocab padding excluded, + ``org_vocab_start_index``), else the original method, else the argmax of
+    the original logits with the padding masked."""
+    out = int8_head(model, hidden_states, want_logits=False)
+    if out is not None:
+        return out[2]
+    if orig_top is not None:
+        return orig_top(model, hidden_states)
+    logits = orig_logits(model, hidden_states)
+    si = model.lm_head.shard_indices
+    if si.num_org_vocab_padding > 0:
+        logits[..., -si.num_org_vocab_padding:] = -float("inf")
+    return logits.argmax(dim=-1) + si.org_vocab_start_index
+
+
 def patch_draft_lm_head() -> bool:
     """MTP drafting through an int8 per-row copy of the lm_head: half the bytes of the bf16 head per draft
     token, and argmax / logsumexp fused into the GEMM."""
@@ -185,22 +216,10 @@ def patch_draft_lm_head() -> bool:
     orig_top = getattr(cls, "get_top_tokens", None)
 
     def compute_logits(self, hidden_states, spec_step_idx=0):
-        out = int8_head(self, hidden_states)
-        if out is None:
-            return orig_logits(self, hidden_states, spec_step_idx)
-        return out[0][..., : self.logits_processor.org_vocab_size]
+        return draft_compute_logits(self, hidden_states, spec_step_idx, orig_logits)
 
     def get_top_tokens(self, hidden_states):
-        out = int8_head(self, hidden_states, want_logits=False)
-        if out is not None:
-            return out[2]
-        if orig_top is not None:
-            return orig_top(self, hidden_states)
-        logits = orig_logits(self, hidden_states)
-        si = self.lm_head.shard_indices
-        if si.num_org_vocab_padding > 0:
-            logits[..., -si.num_org_vocab_padding:] = -float("inf")
-        return logits.argmax(dim=-1) + si.org_vocab_start_index
+        return draft_get_top_tokens(self, hidden_states, orig_logits, orig_top)
 
     compute_logits._qwen_fastpath = True
     get_top_tokens._qwen_fastpath = True

@@ -24,10 +24,13 @@ from ._lib import LIB, check
 
 SMALL_M = 16  # rows handled by the small-M path (w8a16.py:12); larger M keeps vLLM's int8 tensor-core GEMM
 
-# (BLOCK_M, BLOCK_N, BLOCK_K, SPLIT_K, num_warps, num_stages) in the reference's tuple order.  On B200 one
-# configuration serves every shape: 128 output channels x 128 k per pipeline stage, stream-K split over all
-# SMs (SPLIT_K = 0 means "chosen per launch by the stream-K partition"), 8 consumer warps + 1 TMA producer.
-B200_CONFIG = (16, 128, 128, 0, 9, 5)
+# The reference's ``pick_config`` returns a Triton launch tuple (BLOCK_M, BLOCK_N, BLOCK_K, SPLIT_K, num_warps,
+# num_stages) or None.  The B200 library chooses its tile shape, grid and split per call in C++ (pick_tiles in
+# csrc/qf_w8a16.cu: 128x256, 64x512 or 32x1024 output rows x k bytes per stage, data-parallel or stream-K over the
+# SMs, 10 warps); the tuple below only marks a shape as eligible and keeps the reference's return type.  Its
+# entries are BLOCK_M = 16 rows, BLOCK_N = 128 (largest tile height), BLOCK_K = 256, SPLIT_K = 0 ("chosen per
+# launch"), 10 warps, 0 (ring depth chosen per tile shape).
+B200_CONFIG = (16, 128, 256, 0, 10, 0)
 _PDL_DEFAULT = os.environ.get("QF_PDL", "0") == "1"
 
 

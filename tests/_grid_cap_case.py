@@ -1,7 +1,8 @@
-"""Run as ``python -m tests._grid_cap_case`` with QF_GRID_CAP, QF_TILES or QF_SK_SKEW set: GEMM and head shapes
-whose tiles are split between CTAs in ways the full grid never produces (one CTA, a few CTAs, stream-K shares of
-many stages, even or skewed shares where every tile is split), or run on a forced tile shape, checked against the
-oracle.  Exits non-zero on a mismatch.  Used by test_gpu_schedule.py."""
+"""Run as ``python -m tests._grid_cap_case`` with QF_TEST_OVERRIDES=1 and QF_GRID_CAP, QF_TILES, QF_SK_SKEW,
+QF_PEER_WAIT_NS or QF_F16_PATH set: GEMM and head shapes whose tiles are split between CTAs in ways the full grid
+never produces (one CTA, a few CTAs, stream-K shares of many stages, even or skewed shares where every tile is split),
+run on a forced tile shape, or on the all-bf16 activation path, checked against the oracle.  Exits non-zero on a
+mismatch.  Used by test_gpu_schedule.py."""
 from __future__ import annotations
 
 import sys

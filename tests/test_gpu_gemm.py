@@ -39,6 +39,23 @@ def bf16_close(a_bits, b_bits, max_mismatch_frac=0.01):
     return frac
 
 
+def bias_close(got_bits, x_bits, W, s, b_bits, max_mismatch_frac=0.01):
+    """bf16(bf16(acc * s) + bias), the reference's two roundings (patches.py:96-97): a one-ulp difference of the
+    pre-bias value (fp32 summation order) is carried into the sum unchanged, so the tolerance is one ulp of the
+    pre-bias value plus one ulp of the result (plus the accumulation noise of bf16_close)."""
+    pre_bits = orc.w8a16_mm(x_bits, W, s, "bf16")
+    pre = orc.bf16_to_f32(pre_bits).astype(np.float64)
+    ref_bits = orc.add_bias_bf16(pre_bits, b_bits)
+    a = orc.bf16_to_f32(got_bits).astype(np.float64)
+    b = orc.bf16_to_f32(ref_bits).astype(np.float64)
+    ulp = lambda v: np.spacing(np.abs(v).astype(np.float32)).astype(np.float64) * 2.0 ** 16  # noqa: E731
+    tol = ulp(pre) + ulp(np.maximum(np.abs(a), np.abs(b))) + 2.0 ** -16 * np.abs(pre).max()
+    diff = np.abs(a - b)
+    assert not (diff > tol).any(), f"{int((diff > tol).sum())} outputs beyond tolerance; worst {diff.max()}"
+    assert float(np.mean(np.asarray(got_bits) != ref_bits)) <= max_mismatch_frac
+    assert diff.max() / max(np.abs(b).max(), 1e-30) <= 2e-2
+
+
 def run_case(dev, M, N, K, seed, ldx=None, ldw=None, out_dtype="bf16", bias=False, x_bits=None, W=None, s=None):
     import torch
     from qwen_a100_fastpath_b200.w8a16 import pick_config, w8a16_mm
@@ -106,7 +123,7 @@ def test_fp32_accumulator_parity(dev, N, K, M):
 @pytest.mark.parametrize("N,K,M", [(384, 512, 6), (5120, 5120, 5)])
 def test_bias_rounds_like_reference(dev, N, K, M):
     x, W, s, b, y = run_case(dev, M, N, K, seed=77, bias=True)
-    bf16_close(from_dev_bf16(y), orc.qf_int8_linear(x, W, s, b))
+    bias_close(from_dev_bf16(y), x, W, s, b)
 
 
 def test_golden_reference_outputs(dev):

@@ -91,6 +91,14 @@ def test_full_vocab_config3(dev, M):
     torch.backends.cuda.matmul.allow_tf32 = False
     ref = torch.cat([F.linear(x.float(), W[i:i + 8192].float() * s[i:i + 8192, None]) for i in range(0, V, 8192)], 1)
     assert ((lf - ref).norm() / ref.norm()).item() < 3e-3
+    # the draft argmax is the reference's: the argmax of the fp32 dequant-matmul logits rounded to bf16, wherever
+    # their top-2 gap exceeds one bf16 ulp of the top logit (closer pairs are decided by fp32 summation order)
+    rb = ref.to(torch.bfloat16).float()
+    top2 = rb.topk(2, dim=-1).values
+    ulp = (top2[:, 0].abs() * 2.0 ** -7).clamp_min(2.0 ** -133)
+    clear = (top2[:, 0] - top2[:, 1]) > ulp
+    assert clear.any()
+    assert torch.equal(am[clear], rb.argmax(-1)[clear])
 
 
 def test_head_deterministic(dev):
