@@ -178,6 +178,12 @@ int qf_allreduce_bf16(const void* in, void* out, int count, int max_count, int r
                       void* const* bufs, unsigned flags, void* stream);
 /* Reads and clears the sticky error word of this rank's buffer (synchronises `stream`). */
 int qf_allreduce_status(void* own_buf, void* stream, int* status);
+/* Bound of every wait on the other ranks in calls on this rank's buffer (qf_allreduce_bf16 and
+ * qf_w8a16_gemm_allreduce), in microseconds; 0 restores the default of 2 s.  Stored in the buffer's header
+ * (synchronises `stream`), so it also holds for calls captured in a CUDA graph.  An expired wait records
+ * QF_ERR_TIMEOUT (qf_allreduce_status) and the kernel finishes without the missing contributions.  No counterpart
+ * in the reference. */
+int qf_allreduce_set_wait(void* own_buf, unsigned wait_us, void* stream);
 
 /* Row-parallel W8A16 GEMM with the all-reduce fused into its epilogue: y = bf16( sum over ranks r, in rank order, of
  * bf16(scale * x_r . w_r) ) on every rank, where each rank holds its K-shard of x and w (vLLM's RowParallelLinear

@@ -58,6 +58,7 @@ SIGNATURES = [
      [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(_c.c_void_p), _c.c_uint,
       _c.c_void_p]),
     ("qf_allreduce_status", _c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(_c.c_int)]),
+    ("qf_allreduce_set_wait", _c.c_int, [_c.c_void_p, _c.c_uint, _c.c_void_p]),
     ("qf_w8a16_gemm_allreduce", _c.c_int,
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int, _c.c_int,
       _c.c_int, _c.c_void_p, _c.c_size_t, _c.c_int, _c.c_int, _c.POINTER(_c.c_void_p), _c.c_int, _c.c_uint,

@@ -17,8 +17,9 @@
 // Epochs live in device memory (the buffer header), so the call is CUDA-graph capturable: each launch reads
 // epoch = header.epoch + 1 and the last CTA to finish stores it back.  Lines are double-buffered by epoch parity: a
 // rank reaches epoch e + 2 only after every rank has written its lines of epoch e + 1, i.e. finished reading epoch
-// e, so a line is never overwritten while a peer still reads it.  A wait that exceeds kArWaitNs records
-// QF_ERR_TIMEOUT in the header (read by qf_allreduce_status) and the CTA continues.
+// e, so a line is never overwritten while a peer still reads it.  A wait that exceeds its bound (2 s, or what
+// qf_allreduce_set_wait stored in the header) records QF_ERR_TIMEOUT in the header (read by qf_allreduce_status) and
+// the CTA continues.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -56,13 +57,16 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p)
   uint8_t* own = p.bufs[p.rank];
   uint32_t* hdr = reinterpret_cast<uint32_t*>(own);
   __shared__ uint32_t s_epoch;
+  __shared__ uint64_t s_bound;
   __shared__ int s_timeout;
   if (threadIdx.x == 0) {
     s_epoch = *reinterpret_cast<volatile uint32_t*>(hdr + 1) + 1u;
+    s_bound = ar_wait_bound_ns(own);
     s_timeout = 0;
   }
   __syncthreads();
   const uint32_t epoch = s_epoch;
+  const uint64_t bound = s_bound;
   const int par = static_cast<int>(epoch & 1u);
   const int e0 = blockIdx.x * kArChunk;
   const int nl = min(kArChunk, p.count - e0) / 4;  // lines (4 elements each) in this chunk
@@ -82,8 +86,8 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p)
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     for (int r = 0; r < p.world; ++r) {
       const uint2 v = (r == p.rank) ? src[i]
-                                    : ar_wait_line(ar_line(own, par, r, p.max_count, e0 / 4 + i), epoch, &deadline,
-                                                   &timed_out);
+                                    : ar_wait_line(ar_line(own, par, r, p.max_count, e0 / 4 + i), epoch, bound,
+                                                   &deadline, &timed_out);
       bf16x2_acc(a0, a1, v.x);
       bf16x2_acc(a2, a3, v.y);
     }
@@ -197,6 +201,15 @@ int qf_allreduce_bf16(const void* in, void* out, int count, int max_count, int r
   cfg.numAttrs = (flags & QF_FLAG_PDL) ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, allreduce_kernel, p);
   return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, std::string("launch: ") + cudaGetErrorString(e));
+}
+
+int qf_allreduce_set_wait(void* own_buf, unsigned wait_us, void* stream) {
+  if (!own_buf) return fail(QF_ERR_INVALID, "null buffer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint32_t v = wait_us;
+  cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(own_buf) + 12, &v, sizeof(v), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, cudaGetErrorString(e));
 }
 
 int qf_allreduce_status(void* own_buf, void* stream, int* status) {

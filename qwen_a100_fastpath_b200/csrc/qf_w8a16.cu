@@ -418,7 +418,7 @@ __device__ __forceinline__ MaxArg ma_shfl_xor(const MaxArg& v, int mask) {
 // order in fp32 (this rank's from sOut), round once to bf16 and store y.  Every rank computes the same bits.
 template <int BN>
 __device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int lane, const __nv_bfloat16* sOut,
-                                                  uint32_t epoch) {
+                                                  uint32_t epoch, uint64_t bound_ns) {
   constexpr int OS = BN + 8;
   constexpr int LPR = BN / 4;  // lines per token row of the tile
   const int par = static_cast<int>(epoch & 1u);
@@ -443,7 +443,8 @@ __device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int
     for (int r = 0; r < p.ar_world; ++r) {
       const uint2 v = (r == p.ar_rank)
                           ? *reinterpret_cast<const uint2*>(sOut + m * OS + col)
-                          : ar_wait_line(ar_line(own, par, r, p.ar_max_count, l0 + idx), epoch, &deadline, &timed_out);
+                          : ar_wait_line(ar_line(own, par, r, p.ar_max_count, l0 + idx), epoch, bound_ns, &deadline,
+                                         &timed_out);
       bf16x2_acc(a0, a1, v.x);
       bf16x2_acc(a2, a3, v.y);
     }
@@ -469,7 +470,7 @@ __device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int
 template <int BN, int NT, int HEAD, bool AR, bool SILU>
 __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int lane, int c_first, int c_last,
                                                  int* counters, const float* partials, float4* sTile,
-                                                 __nv_bfloat16* sOut, uint32_t ar_epoch) {
+                                                 __nv_bfloat16* sOut, uint32_t ar_epoch, uint64_t ar_bound) {
   // Slot = [BN rows][8*NT tokens] fp32, read as float4: lane takes float4 f = lane + 32 j (row f / (2 NT),
   // tokens 4 (lane % (2 NT)) + 0..3).  All of a contributor's loads (and those of U contributors) are issued
   // before they are added, in ascending CTA order.
@@ -560,7 +561,7 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
   }
   if constexpr (AR) {
     __syncwarp();
-    ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch);
+    ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch, ar_bound);
   } else if constexpr (SILU) {
     __syncwarp();
     silu_mul_store<BN>(p, tile, lane, sOut);
@@ -576,7 +577,7 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
 template <int BN, int NT, int HEAD, bool AR, bool SILU>
 __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane, const float (&v)[BN / 16][NT][4],
                                             const float (&sc)[BN / 16][2], __nv_bfloat16* sOut, float4* sTile,
-                                            uint32_t ar_epoch) {
+                                            uint32_t ar_epoch, uint64_t ar_bound) {
   constexpr int MT = BN / 16;
   constexpr int OS = BN + 8;
   const int g = lane >> 2;
@@ -639,7 +640,7 @@ __device__ __forceinline__ void finish_tile(const Params& p, int tile, int lane,
   __nv_bfloat16* dst = HEAD ? p.logits : static_cast<__nv_bfloat16*>(p.y);
   const int64_t ld = HEAD ? p.ldl : p.ldy;
   if constexpr (AR) {
-    ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch);
+    ar_publish_reduce<BN>(p, tile, lane, sOut, ar_epoch, ar_bound);
   } else if constexpr (SILU) {
     silu_mul_store<BN>(p, tile, lane, sOut);
   } else if (dst) {
@@ -1041,10 +1042,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     uint32_t ar_epoch = 0;  // fused all-reduce: this call's epoch (previous calls on these buffers + 1)
+    uint64_t ar_bound = 0;  // and the bound of its waits on the other ranks
     if constexpr (AR) {
       uint32_t e = 0;
       if (lane == 0) e = *reinterpret_cast<volatile uint32_t*>(p.ar_bufs[p.ar_rank] + 4) + 1u;
       ar_epoch = __shfl_sync(0xffffffffu, e, 0);
+      ar_bound = ar_wait_bound_ns(p.ar_bufs[p.ar_rank]);
     }
     StageIter et = it;
     int tcount = 0;
@@ -1179,12 +1182,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                  static_cast<uint32_t>(c_last - c_first);
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          split_reduce_all<BN, NT, HEAD, AR, SILU>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut, ar_epoch);
+          split_reduce_all<BN, NT, HEAD, AR, SILU>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut, ar_epoch,
+                                                   ar_bound);
           if constexpr (HEAD) fold_tile<HEAD>(p, lane, sStat, run, run_z);
         }
         continue;
       }
-      finish_tile<BN, NT, HEAD, AR, SILU>(p, tile, lane, v, sc, sOut, sStat, ar_epoch);
+      finish_tile<BN, NT, HEAD, AR, SILU>(p, tile, lane, v, sc, sOut, sStat, ar_epoch, ar_bound);
       if constexpr (HEAD) fold_tile<HEAD>(p, lane, sStat, run, run_z);
     }
     if (AR && lane == 0) {  // the last CTA to finish advances the buffers' epoch for the next call

@@ -119,6 +119,11 @@ class NVLinkAllReduce:
             self.own, torch.cuda.current_stream().cuda_stream, self._ct.byref(st)))
         return st.value
 
+    def set_wait(self, wait_us: int) -> None:
+        """Bound of this rank's waits on the other ranks, in microseconds (0: the default 2 s); synchronises."""
+        self._check("qf_allreduce_set_wait", self._lib.qf_allreduce_set_wait(
+            self.own, int(wait_us), torch.cuda.current_stream().cuda_stream))
+
     def close(self) -> None:
         """Collective: unmap the other ranks' buffers, wait for every rank, free this rank's buffer."""
         if self.own is None:
