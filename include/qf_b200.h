@@ -137,6 +137,21 @@ int qf_w8a16_noalloc_status(void* stream, int* status);
 int qf_w8a16_gemm_silu_mul(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,
                            int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, unsigned flags, void* stream);
 
+/* ---- prefill (M > 16): dynamic per-token int8 activations x int8 weights on tcgen05 ----------------------------
+ * Replaces the W8A8 fallback of qf_int8_linear for the rows the small-M path does not take
+ * (plugin/qwen_fastpath/patches.py:99-100: vLLM's scaled_int8_quant + cutlass_scaled_mm, vllm==0.31.0):
+ *   s_x[m] = max_k |x[m,k]| / 127,  q[m,k] = round_half_even_saturate_s8( x[m,k] * (127 / max_k |x[m,k]|) ),
+ *   y[m,n] = bf16( s_x[m] * (w_scale[n] * float(sum_k q[m,k] * w[n,k])) ), with a bias: bf16( fma(s_x[m], t, bias[n]) ).
+ * x bf16 [M, K] (row stride ldx, 2-byte aligned; 16-byte loads when 16-byte aligned with ldx % 8 == 0); w, w_scale,
+ * bias, y as qf_w8a16_gemm (y bf16).  Any M >= 1.  The workspace (>= qf_w8a8_workspace_bytes(M, K), 256-byte aligned)
+ * holds a 256-byte header (word 0: sticky error flag, see qf_workspace_status), then q int8 [M, ldq] with
+ * ldq = K rounded up to 16, padded to 256 bytes, then s_x fp32 [M].  Two launches on `stream`: the quantization
+ * (with QF_FLAG_PDL it may overlap the previous kernel's tail) and the GEMM (its first weight copies overlap the
+ * quantization). */
+size_t qf_w8a8_workspace_bytes(int M, int K);
+int qf_w8a8_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* w_scale, const void* bias,
+                 void* y, int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, unsigned flags, void* stream);
+
 /* Load-time int8 quantizer of the draft LM head on the device: replaces the per-row symmetric quantizer the
  * reference runs in torch when the drafter loads (plugin/qwen_fastpath/patches.py:143-147).  w: bf16 [V, H] (row
  * stride ldw elements); q: int8 [V, H] (row stride ldq bytes); scale: fp32 [V].  s = max(max|w|, 1e-8) / 127,

@@ -16,7 +16,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIB = PKG / "libqf_b200.so"
-SOURCES = ["qf_w8a16.cu", "qf_allreduce.cu", "qf_quant.cu"]
+SOURCES = ["qf_w8a16.cu", "qf_allreduce.cu", "qf_quant.cu", "qf_w8a8.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

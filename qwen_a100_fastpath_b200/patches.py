@@ -5,9 +5,11 @@ Same patch targets, guards and fallbacks as ``qwen_fastpath.patches`` of EurekaZ
 
 * ``patch_int8_linear``: ``CutlassInt8ScaledMMLinearKernel.apply_weights(self, layer, x, bias=None)`` routes
   dynamic symmetric per-token W8A8 linears (patches.py:110) to the opaque custom op
-  ``torch.ops.vllm.qf_int8_linear(x, w_q, w_s, bias)`` (patches.py:84-106).  ``M <= 16`` bf16 rows on a
-  K-major weight with per-channel scales take the B200 kernel (bias fused, rounded like the reference's
-  ``y + bias``); everything else keeps vLLM's CUTLASS W8A8 path (patches.py:99-101).
+  ``torch.ops.vllm.qf_int8_linear(x, w_q, w_s, bias)`` (patches.py:84-106).  bf16 rows on a K-major weight with
+  per-channel scales run on libqf_b200: ``M <= 16`` on the W8A16 kernel (bias fused, rounded like the reference's
+  ``y + bias``), more rows (prefill) on the tcgen05 W8A8 kernel with the arithmetic of the reference's vLLM
+  fallback (patches.py:99-101); anything else (fp16 activations, weights the tensor maps cannot take) keeps
+  vLLM's CUTLASS W8A8 path.
 * ``patch_draft_lm_head``: an int8 per-row copy of the MTP draft lm_head made at load time
   (patches.py:133-152), ``compute_logits`` through the int8 head (patches.py:157-174), and ``get_top_tokens``
   taken from the head kernel's fused argmax (patches.py:176-185), which also yields the per-row logsumexp
@@ -38,8 +40,12 @@ def w8a8_fallback(x2: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor, bias: 
 
 
 def make_int8_linear_op():
-    """The ``qf_int8_linear`` implementation and its fake (shape-only) counterpart."""
-    from .w8a16 import SMALL_M, pick_config, w8a16_mm, weight_supported
+    """The ``qf_int8_linear`` implementation and its fake (shape-only) counterpart.
+
+    bf16 activations on a K-major int8 weight with per-channel scales run on libqf_b200: ``M <= 16`` rows on the
+    small-M W8A16 kernel (the reference's path), more rows on the tcgen05 W8A8 kernel with the reference's own
+    fallback arithmetic (per-token int8 activations, scaled int32 GEMM).  Anything else keeps vLLM's path."""
+    from .w8a16 import SMALL_M, pick_config, w8a8_mm, w8a16_mm, weight_supported
 
     def qf_int8_linear(x: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor,
                        bias: torch.Tensor | None) -> torch.Tensor:
@@ -47,11 +53,13 @@ def make_int8_linear_op():
         x2 = x.reshape(-1, x.shape[-1])
         M, K = x2.shape
         N = w_q.shape[1]
-        if (M <= SMALL_M and x2.dtype == torch.bfloat16 and w_q.stride(0) == 1 and w_s.numel() == N
-                and weight_supported(w_q)):
+        if x2.dtype == torch.bfloat16 and w_q.stride(0) == 1 and w_s.numel() == N and weight_supported(w_q):
             cfg = pick_config(N, K)
             if cfg is not None:
-                y = w8a16_mm(x2, w_q, w_s, cfg, x.dtype, bias=bias, pdl=True)
+                if M <= SMALL_M:
+                    y = w8a16_mm(x2, w_q, w_s, cfg, x.dtype, bias=bias, pdl=True)
+                else:
+                    y = w8a8_mm(x2, w_q, w_s, bias=bias, pdl=True)
                 return y.view(*lead, N)
         return w8a8_fallback(x2, w_q, w_s, bias, x.dtype).view(*lead, N)
 

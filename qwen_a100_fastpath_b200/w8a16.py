@@ -317,3 +317,73 @@ def w8a16_head_sample(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor,
                                   ws.data_ptr(), ws.numel(), flags, stream.cuda_stream)
     check("qf_w8a16_head_sample", rc)
     return logits, row_max, row_arg, row_lse, sample, score, slogit
+
+
+# ----------------------------------------------------------------------------------------------
+# prefill (M > 16): per-token int8 activations x int8 weights on tcgen05 (qf_w8a8_gemm)
+# ----------------------------------------------------------------------------------------------
+_pf_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _prefill_workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream.cuda_stream)
+    with _ws_lock:
+        buf = _pf_ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _pf_ws[key] = buf
+        return buf
+
+
+def w8a8_mm(x: torch.Tensor, w_t: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
+            out: torch.Tensor | None = None, pdl: bool | None = None) -> torch.Tensor:
+    """``x [M, K]`` bf16 (any M) quantized per token to int8 and multiplied with ``w_t [K, N]`` int8 (stride
+    ``(1, ldw)``) on the tensor cores: ``y = bf16(s_x[m] * (w_scale[n] * acc[m, n]) (+ bias))`` -- what the reference's
+    ``qf_int8_linear`` gets from vLLM's ``scaled_int8_quant`` + ``cutlass_scaled_mm`` for the rows its small-M
+    kernel does not take (plugin/qwen_fastpath/patches.py:99-100)."""
+    if x.dim() != 2:
+        raise ValueError("x must be 2-D [M, K]")
+    M, K = x.shape
+    N = w_t.shape[1]
+    if w_t.shape[0] != K or K < 1:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} vs w_t {tuple(w_t.shape)}")
+    if not (x.is_cuda and w_t.is_cuda and w_scale.is_cuda) or x.dtype != torch.bfloat16:
+        raise ValueError("libqf_b200 needs CUDA tensors and bf16 activations (there is no CPU path)")
+    scale = w_scale.reshape(-1)
+    if scale.numel() != N or scale.dtype != torch.float32:
+        raise ValueError("w_scale must hold N fp32 per-channel scales")
+    scale = scale.contiguous()
+    if bias is not None:
+        if bias.numel() != N or bias.dtype != torch.bfloat16:
+            raise ValueError("bias must be bf16 [N]")
+        bias = bias.reshape(-1).contiguous()
+    ldw = _check_weight(w_t, K)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    elif out.shape != (M, N) or out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError("out must be bf16 [M, N] with unit column stride")
+    if M == 0 or N == 0:
+        return out
+    stream = torch.cuda.current_stream(x.device)
+    ws = _prefill_workspace(x.device, stream, LIB.qf_w8a8_workspace_bytes(M, K))
+    flags = _lib.QF_FLAG_PDL if (_PDL_DEFAULT if pdl is None else pdl) else 0
+    rc = LIB.qf_w8a8_gemm(x.data_ptr(), x.stride(0), w_t.data_ptr(), ldw, scale.data_ptr(),
+                          bias.data_ptr() if bias is not None else None, out.data_ptr(), out.stride(0), M, N, K,
+                          ws.data_ptr(), ws.numel(), flags, stream.cuda_stream)
+    check("qf_w8a8_gemm", rc)
+    return out
+
+
+def prefill_workspace_status(device=None, stream=None) -> int:
+    """Read and clear the sticky device error flag of the current stream's prefill workspace (synchronises)."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    stream = torch.cuda.current_stream(device) if stream is None else stream
+    buf = _pf_ws.get((device.index, stream.cuda_stream))
+    if buf is None:
+        return _lib.QF_OK
+    import ctypes
+    st = ctypes.c_int(0)
+    check("qf_workspace_status", LIB.qf_workspace_status(buf.data_ptr(), stream.cuda_stream, ctypes.byref(st)))
+    return st.value

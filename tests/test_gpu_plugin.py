@@ -3,11 +3,11 @@ reference) and the patched draft-head hooks ``compute_logits`` / ``get_top_token
 CUDA tensors and checked against the oracle.
 
 Covered: 3-D ``[B, T, K]`` input flattened to rows, a bias rounded like the reference's ``y + bias``, activation rows
-with a stride, M = 1, 5 and 16 on the BASELINE config-2 shapes, and the gate that sends M = 17, fp16 activations and a
-weight view the tensor maps cannot take to vLLM's W8A8 path (replaced here by a sentinel, so the routing is checked
-without vLLM's compiled kernels).  The hooks are driven with a fake drafter on the GPU: vocab padding, a nonzero
-``org_vocab_start_index``, the ``org_vocab_size`` slice, and the fallbacks to the original methods.  Tolerances as the
-GEMM tests (one bf16 ulp plus 2^-16 max|y|, at most 1 % of outputs differing; with a bias, plus one ulp of the pre-bias
+with a stride, M = 1, 5 and 16 on the BASELINE config-2 shapes, and the gate: M = 17 rows take the prefill kernel,
+fp16 activations and a weight view the tensor maps cannot take go to vLLM's W8A8 path (replaced here by a sentinel,
+so the routing is checked without vLLM's compiled kernels).  The hooks are driven with a fake drafter on the GPU:
+vocab padding, a nonzero ``org_vocab_start_index``, the ``org_vocab_size`` slice, and the fallbacks to the original
+methods.  Tolerances as the GEMM tests (one bf16 ulp plus 2^-16 max|y|, at most 1 % of outputs differing; with a bias, plus one ulp of the pre-bias
 value); argmax exact.
 """
 from __future__ import annotations
@@ -103,20 +103,27 @@ def test_op_strided_rows(dev, op, fallback):
     bf16_close(from_dev_bf16(y2), orc.qf_int8_linear(x_bits[:3], W, s))
 
 
-def test_op_gate_routes_to_w8a8(dev, op, fallback):
+def test_op_gate(dev, op, fallback):
+    """M = 17 bf16 rows take the prefill kernel; fp16 activations and a weight the tensor maps cannot take go to
+    vLLM's W8A8 path; eligible small-M calls stay on the decode kernel."""
     import torch
+    from oracle import w8a8_oracle as pre
     N, K = 1024, 512
     x_bits, W, s, w_q, w_s = weights(dev, N, K, 24)
-    x17 = torch.randn(17, K, device=dev).to(torch.bfloat16)
-    assert op(x17, w_q, w_s, None).shape == (17, N)                   # M > SMALL_M
+    x17_bits = orc.make_inputs(25, 17, 8, K)[0]
+    y17 = op(to_dev_bf16(x17_bits, dev), w_q, w_s, None)              # M > SMALL_M: the prefill kernel
+    torch.cuda.synchronize()
+    assert not fallback
+    assert np.array_equal(from_dev_bf16(y17), pre.w8a8_mm(x17_bits, W, s))
     x16 = to_dev_bf16(x_bits, dev)
     assert op(x16.half(), w_q, w_s, None).dtype == torch.float16      # fp16 activations
     raw = torch.zeros(N * K + 8, dtype=torch.int8, device=dev)
     w_mis = raw[8:].view(N, K).t()                                    # base 8 bytes off a 16-byte boundary
     assert w_mis.stride(0) == 1 and w_mis.data_ptr() % 16 != 0
     op(x16[:4], w_mis, w_s, None)
-    assert [c[0] for c in fallback] == [(17, K), (16, K), (4, K)]
-    assert fallback[1][2] == torch.float16
+    op(to_dev_bf16(x17_bits, dev), w_mis, w_s, None)                  # also above 16 rows
+    assert [c[0] for c in fallback] == [(16, K), (4, K), (17, K)]
+    assert fallback[0][2] == torch.float16
     y = op(x16[:4], w_q, w_s, None)                                   # and the eligible call stays on the kernel
     torch.cuda.synchronize()
     assert len(fallback) == 3
