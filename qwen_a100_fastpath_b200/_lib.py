@@ -102,3 +102,20 @@ LIB = _load()
 def check(fn: str, code: int) -> None:
     if code != QF_OK:
         raise QFError(fn, code)
+
+
+TORCH_OPS_PATH = Path(__file__).resolve().parent / "_qf_torch_ops.so"
+_torch_ops_loaded = False
+
+
+def load_torch_ops():
+    """Registers ``torch.ops.qf_b200.int8_linear`` (the PyTorch operator over this C ABI, csrc/qf_torch_ops.cpp);
+    raises if it is not built.  Returns the op."""
+    global _torch_ops_loaded
+    import torch
+    if not _torch_ops_loaded:
+        if not TORCH_OPS_PATH.exists():
+            raise ImportError(f"{TORCH_OPS_PATH.name} is not built; run `python -m qwen_a100_fastpath_b200.build`")
+        torch.ops.load_library(str(TORCH_OPS_PATH))
+        _torch_ops_loaded = True
+    return torch.ops.qf_b200.int8_linear

@@ -898,6 +898,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cta = blockIdx.x;
 
   if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmap_w);
+    prefetch_tensormap(&tmap_x);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kConsumerWarps);  // one arrival per consumer warp
@@ -906,18 +908,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     *sLast = 0;
     *sCoop = 0;
     fence_mbar_init();
-  }
-  {
-    // Token rows M .. 8*NT-1 of every activation box are never written by the copies (the boxes are M rows high):
-    // zero them once so that those MMA columns compute zeros.
-    const int zrows = 8 * NT - p.M;
-    const int per_box = zrows * 8;  // 16-byte units
-    for (int idx = threadIdx.x; idx < S * 2 * B * per_box; idx += kThreads) {
-      const int box = idx / per_box;
-      const int rem = idx - box * per_box;
-      *reinterpret_cast<uint4*>(sX + box * C::kXBoxBytes + (p.M + rem / 8) * 128 + (rem % 8) * 16) =
-          make_uint4(0u, 0u, 0u, 0u);
-    }
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -930,11 +920,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int sk_t1 = it.n_sk > 0 ? (it.sk_end - 1) / p.kiters : -1;
 
   if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ producer (one lane)
+    // ------------------------------------------------------------------ producer (lanes 0 and 1)
+    // Lane 0 issues the weight boxes of the first S stages before griddepcontrol.wait (weights are never written by
+    // the previous kernel), then every later stage.  Lane 1 waits for the previous kernel and at once issues the
+    // activation boxes of those first stages, so they do not queue behind lane 0's weight copies.  Both arrive on the
+    // same full barriers: the stage completes when lane 0's arrive.expect_tx (of the stage's weight + activation
+    // bytes) has happened and all those bytes have landed, whichever lane's copies land first.
+    const int npre = n_iter < S ? n_iter : S;
+    if (lane == 1) {
+      const uint64_t pol_x = policy_evict_last();
+      pdl_wait();
+      StageIter xi = it;
+      for (int i = 0; i < npre; ++i) {
+        uint8_t* xs = sX + i * C::kXStageBytes;
+#pragma unroll
+        for (int b = 0; b < 2 * B; ++b)
+          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * KS + b * 64, 0, pol_x);
+        xi.next(p);
+      }
+    }
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
-      const int npre = n_iter < S ? n_iter : S;
       StageIter pi = it;
       for (int i = 0; i < npre; ++i) {  // weights do not depend on the previous kernel
         mbar_arrive_expect_tx(&full_bar[i], C::kWBytes + p.x_tx);
@@ -951,15 +958,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pi.next(p);
       }
-      pdl_wait();
-      StageIter xi = it;
-      for (int i = 0; i < npre; ++i) {
-        uint8_t* xs = sX + i * C::kXStageBytes;
-#pragma unroll
-        for (int b = 0; b < 2 * B; ++b)
-          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * KS + b * 64, 0, pol_x);
-        xi.next(p);
-      }
+      pdl_wait();  // this lane issues activation boxes from stage S on
       int issued = npre;
       for (int i = npre; i < n_iter; ++i) {
         const int s = i % S;
@@ -1209,6 +1208,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // -------------------------------------------------------------------- consumers (8 warps)
+  {
+    // Token rows M .. 8*NT-1 of every activation box are never written by the copies (the boxes are M rows high):
+    // zero them once so that those MMA columns compute zeros.  The copies write only rows < M of the same boxes.
+    const int zrows = 8 * NT - p.M;
+    const int per_box = zrows * 8;  // 16-byte units
+    for (int idx = threadIdx.x; idx < S * 2 * B * per_box; idx += kConsumerThreads) {
+      const int box = idx / per_box;
+      const int rem = idx - box * per_box;
+      *reinterpret_cast<uint4*>(sX + box * C::kXBoxBytes + (p.M + rem / 8) * 128 + (rem % 8) * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+  }
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
   // Warp (u, h), u = warp / 2: m-tile group mg = u % NMW (m-tiles MW * mg ..), weight boxes
   // b = u / NMW + j * (4 / NMW), j < BPW.

@@ -45,23 +45,20 @@ def make_int8_linear_op():
     bf16 activations on a K-major int8 weight with per-channel scales run on libqf_b200: ``M <= 16`` rows on the
     small-M W8A16 kernel (the reference's path), more rows on the tcgen05 W8A8 kernel with the reference's own
     fallback arithmetic (per-token int8 activations, scaled int32 GEMM).  Anything else keeps vLLM's path."""
-    from .w8a16 import SMALL_M, pick_config, w8a8_mm, w8a16_mm, weight_supported
+    from ._lib import QF_MAX_N, load_torch_ops
+    kernel = load_torch_ops()  # torch.ops.qf_b200.int8_linear (csrc/qf_torch_ops.cpp)
+    bf16 = torch.bfloat16
 
     def qf_int8_linear(x: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor,
                        bias: torch.Tensor | None) -> torch.Tensor:
-        lead = x.shape[:-1]
-        x2 = x.reshape(-1, x.shape[-1])
-        M, K = x2.shape
+        # the reference's gate (patches.py:91) without its M limit, plus the tensor-map rules for the weight view
+        # (16-byte base, 16-byte row stride); the operator checks the rest and picks the kernel by M
         N = w_q.shape[1]
-        if x2.dtype == torch.bfloat16 and w_q.stride(0) == 1 and w_s.numel() == N and weight_supported(w_q):
-            cfg = pick_config(N, K)
-            if cfg is not None:
-                if M <= SMALL_M:
-                    y = w8a16_mm(x2, w_q, w_s, cfg, x.dtype, bias=bias, pdl=True)
-                else:
-                    y = w8a8_mm(x2, w_q, w_s, bias=bias, pdl=True)
-                return y.view(*lead, N)
-        return w8a8_fallback(x2, w_q, w_s, bias, x.dtype).view(*lead, N)
+        if (x.dtype is bf16 and w_q.stride(0) == 1 and w_s.numel() == N and 0 < N <= QF_MAX_N and x.shape[-1] > 0
+                and w_q.data_ptr() % 16 == 0 and (N == 1 or w_q.stride(1) % 16 == 0)):
+            return kernel(x, w_q, w_s, bias)
+        x2 = x.reshape(-1, x.shape[-1])
+        return w8a8_fallback(x2, w_q, w_s, bias, x.dtype).view(*x.shape[:-1], N)
 
     def qf_int8_linear_fake(x: torch.Tensor, w_q: torch.Tensor, w_s: torch.Tensor,
                             bias: torch.Tensor | None) -> torch.Tensor:

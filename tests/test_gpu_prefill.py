@@ -112,8 +112,11 @@ def test_prefill_edges(dev, M, N, K, ldx, off, bias):
     x = buf[off:off + M * ld].view(M, ld)[:, :K]
     x.copy_(to_dev_bf16(x_bits, dev))
     b_bits = orc.make_bias(M + N, N) if bias else None
-    y, ws = call(dev, x, torch.from_numpy(W).to(dev), torch.from_numpy(s).to(dev),
-                 bias=to_dev_bf16(b_bits, dev) if bias else None)
+    ldw = (K + 15) // 16 * 16                  # TMA: weight rows padded to a 16-byte stride
+    Wp = np.zeros((N, ldw), np.int8)
+    Wp[:, :K] = W
+    Wd = torch.from_numpy(Wp).to(dev)[:, :K]
+    y, ws = call(dev, x, Wd, torch.from_numpy(s).to(dev), bias=to_dev_bf16(b_bits, dev) if bias else None)
     q, sx = workspace_quant(ws, M, K)
     q_o, sx_o = pre.quantize_tokens(x_bits)
     assert np.array_equal(q, q_o) and np.array_equal(sx.view(np.uint32), sx_o.view(np.uint32))
