@@ -920,26 +920,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int sk_t1 = it.n_sk > 0 ? (it.sk_end - 1) / p.kiters : -1;
 
   if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ producer (lanes 0 and 1)
-    // Lane 0 issues the weight boxes of the first S stages before griddepcontrol.wait (weights are never written by
-    // the previous kernel), then every later stage.  Lane 1 waits for the previous kernel and at once issues the
-    // activation boxes of those first stages, so they do not queue behind lane 0's weight copies.  Both arrive on the
-    // same full barriers: the stage completes when lane 0's arrive.expect_tx (of the stage's weight + activation
-    // bytes) has happened and all those bytes have landed, whichever lane's copies land first.
-    const int npre = n_iter < S ? n_iter : S;
-    if (lane == 1) {
-      const uint64_t pol_x = policy_evict_last();
-      pdl_wait();
-      StageIter xi = it;
-      for (int i = 0; i < npre; ++i) {
-        uint8_t* xs = sX + i * C::kXStageBytes;
-#pragma unroll
-        for (int b = 0; b < 2 * B; ++b)
-          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * KS + b * 64, 0, pol_x);
-        xi.next(p);
-      }
-    }
+    // ------------------------------------------------------------------ producer (one lane)
     if (lane == 0) {
+      const int npre = n_iter < S ? n_iter : S;
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
       StageIter pi = it;
@@ -958,7 +941,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pi.next(p);
       }
-      pdl_wait();  // this lane issues activation boxes from stage S on
+      pdl_wait();
+      StageIter xi = it;
+      for (int i = 0; i < npre; ++i) {
+        uint8_t* xs = sX + i * C::kXStageBytes;
+#pragma unroll
+        for (int b = 0; b < 2 * B; ++b)
+          tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * KS + b * 64, 0, pol_x);
+        xi.next(p);
+      }
       int issued = npre;
       for (int i = npre; i < n_iter; ++i) {
         const int s = i % S;
