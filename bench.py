@@ -67,10 +67,13 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
     ap.add_argument("--sweep-out", default="")
+    ap.add_argument("--prefill-sweep", action="store_true", help="the M > 16 int8 path (qf_w8a8_gemm: per-token "
+                    "quantization + tcgen05 GEMM) on every config-2 GEMM at M = 32..4096, beside torch._int_mm")
     ap.add_argument("--host-overhead", action="store_true", help="eager host time per call of the public entry "
                     "points (enqueue only) against the kernel's device time, o_proj at --m")
-    ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head,lm_head_sample: a few "
-                    "launches of each at --m (the small case for an ncu capture), then exit")
+    ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head,lm_head_sample "
+                    "(or pf_qkv, pf_o_proj, pf_gate_up, pf_down: the prefill path): a few launches of each at --m (the "
+                    "small case for an ncu capture), then exit")
     return ap.parse_args()
 
 
@@ -576,6 +579,9 @@ def run_profile_gemm(args, local: int):
     shapes = {nm: (N, K) for nm, N, K, _ in LAYER + [HEAD]}
     shapes["lm_head_sample"] = shapes["lm_head"]
     g = torch.Generator(device=dev).manual_seed(3)
+    from qwen_a100_fastpath_b200.w8a16 import w8a8_mm
+    for nm, N, K, _ in LAYER:
+        shapes["pf_" + nm] = (N, K)
     for name in args.profile_gemm.split(","):
         N, K = shapes[name]
         x = torch.randn(args.m, K, device=dev, generator=g).to(torch.bfloat16)
@@ -587,11 +593,76 @@ def run_profile_gemm(args, local: int):
                 w8a16_head(x, W.t(), s)
             elif name == "lm_head_sample":
                 w8a16_head_sample(x, W.t(), s, temperature=0.8, seed=1, offset=0)
+            elif name.startswith("pf_"):
+                w8a8_mm(x, W.t(), s)
             else:
                 w8a16_mm(x, W.t(), s, None, torch.bfloat16)
             torch.cuda.synchronize()
             del W
     print("profile-gemm done:", args.profile_gemm)
+
+
+def run_prefill_sweep(args, local: int):
+    """Prefill path (M > 16): qf_w8a8_gemm (per-token int8 quantization of the bf16 activations, then the tcgen05
+    int8 GEMM with the scaled bf16 epilogue) on every config-2 GEMM at M in {32, ..., 4096}; beside it torch._int_mm
+    (cuBLASLt int8 x int8 -> int32, on already-quantized activations, no scaling: a plain library GEMM of the same
+    contraction).  CUDA graph of launches over distinct weight copies (more than 2x L2 per pass); tera-ops/s =
+    2 M N K / time, % of the nominal 4.5 dense int8 POPS (no measured int8 peak on this pool) and GB/s of the weight
+    + activation + output bytes."""
+    import torch
+    from qwen_a100_fastpath_b200.w8a16 import w8a8_mm
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    stream = torch.cuda.Stream(dev)
+    rows = []
+    for name, N, K, _ in LAYER:
+        copies = max(2, int(2 * 126e6 // (N * K)) + 1)
+        Ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g) for _ in range(copies)]
+        Ss = [torch.rand(N, device=dev, generator=g) * 0.009 + 0.001 for _ in range(copies)]
+        for M in (32, 64, 128, 256, 512, 1024, 2048, 4096):
+            x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+            xq = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            res = {}
+            for impl in ("ours", "torch_int_mm"):
+                def call(i, impl=impl):
+                    if impl == "ours":
+                        w8a8_mm(x, Ws[i].t(), Ss[i], out=y, pdl=True)
+                    else:
+                        torch._int_mm(xq, Ws[i].t())
+                try:
+                    with torch.cuda.stream(stream):
+                        for i in range(copies):
+                            call(i)
+                    torch.cuda.synchronize()
+                    reps = max(copies, 8)
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=stream):
+                        for i in range(reps):
+                            call(i % copies)
+                    ms = time_graph(gr, stream, 5, 2) / reps
+                    del gr
+                    res[impl] = ms
+                except Exception as e:  # noqa: BLE001 -- the library comparator may reject a shape
+                    res[impl] = None
+                    print(f"{impl} {name} M={M}: {type(e).__name__}: {str(e)[:120]}", file=sys.stderr)
+            flops = 2.0 * M * N * K
+            nbytes = N * K + 4 * N + 2 * M * K + 2 * M * N
+            row = {"gemm": name, "N": N, "K": K, "M": M}
+            for impl, ms in res.items():
+                if ms is None:
+                    row[impl] = None
+                    continue
+                row[impl] = {"us": round(ms * 1e3, 2), "TOPS": round(flops / (ms * 1e-3) / 1e12, 1),
+                             "frac_int8_nominal": round(flops / (ms * 1e-3) / 4.5e15, 4),
+                             "GBps": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+            rows.append(row)
+            print(json.dumps(row), flush=True)
+        del Ws, Ss
+        torch.cuda.empty_cache()
+    if args.sweep_out:
+        Path(args.sweep_out).write_text(json.dumps(rows, indent=1))
 
 
 def run_host_overhead(args, local: int):
@@ -666,6 +737,10 @@ def main():
     if args.host_overhead:
         if rank == 0:
             run_host_overhead(args, local)
+        return
+    if args.prefill_sweep:
+        if rank == 0:
+            run_prefill_sweep(args, local)
         return
     run_ours(args, rank, world, local)
 
