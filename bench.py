@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--sweep-out", default="")
     ap.add_argument("--prefill-sweep", action="store_true", help="the M > 16 int8 path (qf_w8a8_gemm: per-token "
                     "quantization + tcgen05 GEMM) on every config-2 GEMM at M = 32..4096, beside torch._int_mm")
+    ap.add_argument("--fused-sweep", action="store_true", help="RMSNorm fused into qkv and RMSNorm + SiLU fused into "
+                    "gate_up (qf_w8a16_gemm_rmsnorm) against vLLM's RMSNorm in torch followed by the GEMM, at M = 1..16")
     ap.add_argument("--host-overhead", action="store_true", help="eager host time per call of the public entry "
                     "points (enqueue only) against the kernel's device time, o_proj at --m")
     ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head,lm_head_sample "
@@ -665,6 +667,61 @@ def run_prefill_sweep(args, local: int):
         Path(args.sweep_out).write_text(json.dumps(rows, indent=1))
 
 
+def run_fused_sweep(args, local: int):
+    """qkv with the preceding RMSNorm (input_layernorm, with residual) and gate_up with RMSNorm + SiLU fused
+    (qf_w8a16_gemm_rmsnorm), against the unfused sequence: vLLM's fused_add_rms_norm as its torch expression
+    (vllm/ir/ops/layernorm.py), then w8a16_mm (and, for gate_up, the GEMM with the SiLU gate fused).  CUDA graphs of
+    launches over distinct weight copies; mean us per layer-norm + GEMM."""
+    import torch
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_mm, w8a16_mm_rmsnorm, w8a16_mm_silu_mul
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(13)
+    stream = torch.cuda.Stream(dev)
+    K = 5120
+    gamma = (torch.rand(K, device=dev, generator=g) + 0.5).to(torch.bfloat16)
+    for name, N, silu in (("qkv", 10240, False), ("gate_up", 34816, True)):
+        copies = 8
+        Ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g) for _ in range(copies)]
+        Ss = [torch.rand(N, device=dev, generator=g) * 0.009 + 0.001 for _ in range(copies)]
+        for M in (1, 5, 8, 16):
+            x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+            res = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+            res_out = torch.empty_like(res)
+            y = torch.empty(M, N // 2 if silu else N, device=dev, dtype=torch.bfloat16)
+
+            def unfused(i):
+                z = x.float() + res.float()
+                r = z.to(torch.bfloat16)
+                a = (z * torch.rsqrt(z.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16) * gamma
+                if silu:
+                    w8a16_mm_silu_mul(a, Ws[i].t(), Ss[i], out=y, pdl=True)
+                else:
+                    w8a16_mm(a, Ws[i].t(), Ss[i], None, torch.bfloat16, out=y, pdl=True)
+                return r
+
+            def fused(i):
+                w8a16_mm_rmsnorm(x, gamma, 1e-6, Ws[i].t(), Ss[i], residual=res, silu_mul=silu,
+                                 residual_out=res_out, out=y, pdl=True)
+
+            row = {"gemm": name, "N": N, "K": K, "M": M}
+            for tag, fn in (("unfused_torch_norm_then_gemm", unfused), ("fused", fused)):
+                with torch.cuda.stream(stream):
+                    for i in range(copies):
+                        fn(i)
+                torch.cuda.synchronize()
+                reps = 32
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for i in range(reps):
+                        fn(i % copies)
+                row[tag + "_us"] = round(time_graph(gr, stream, 5, 2) / reps * 1e3, 2)
+                del gr
+            print(json.dumps(row), flush=True)
+        del Ws, Ss
+        torch.cuda.empty_cache()
+
+
 def run_host_overhead(args, local: int):
     """Host cost of one eager call (argument checks, ctypes, tensor-map encoding, launch) of the C-ABI entry point,
     of ``w8a16_mm`` and of the ``qf_int8_linear`` op body, against the device time of the same launch, for o_proj at
@@ -741,6 +798,10 @@ def main():
     if args.prefill_sweep:
         if rank == 0:
             run_prefill_sweep(args, local)
+        return
+    if args.fused_sweep:
+        if rank == 0:
+            run_fused_sweep(args, local)
         return
     run_ours(args, rank, world, local)
 

@@ -152,6 +152,20 @@ size_t qf_w8a8_workspace_bytes(int M, int K);
 int qf_w8a8_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* w_scale, const void* bias,
                  void* y, int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, unsigned flags, void* stream);
 
+/* The W8A16 GEMM with the RMSNorm that precedes qkv and gate_up in a decoder layer fused into it (the reference plugin
+ * leaves the norm to vLLM's RMSNorm: z = x + residual, new residual = bf16(z), normalized activation
+ * bf16(bf16(z * rsqrt(mean(z^2) + eps)) * gamma)).  Here the activation fed to the contraction is bf16(bf16(z) * gamma)
+ * and each token's fp32 accumulators are multiplied by rsqrt(mean(z^2) + eps) (z in fp32) before the scale and the
+ * bf16 rounding: the per-token factor commutes with the k-sum, so only the rounding of the normalized activation
+ * differs from the unfused sequence.  residual: bf16 [M, K] (ldr) or NULL (z = x); gamma: bf16 [K], 16-byte
+ * aligned; residual_out: bf16 [M, K] (ldro) receiving bf16(z), or NULL; it must not overlap x or residual.
+ * silu_mul = 0: y = the GEMM output [M, N]; 1: w is the merged gate_up weight and y = bf16(bf16(silu(g)) * u)
+ * [M, N/2] as qf_w8a16_gemm_silu_mul.  No bias.  K % 8 == 0, K <= 8192; other arguments as qf_w8a16_gemm. */
+int qf_w8a16_gemm_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, const void* gamma, float eps,
+                          void* residual_out, int64_t ldro, const int8_t* w, int64_t ldw, const float* scale, void* y,
+                          int64_t ldy, int M, int N, int K, int silu_mul, void* ws, size_t ws_bytes, unsigned flags,
+                          void* stream);
+
 /* Load-time int8 quantizer of the draft LM head on the device: replaces the per-row symmetric quantizer the
  * reference runs in torch when the drafter loads (plugin/qwen_fastpath/patches.py:143-147).  w: bf16 [V, H] (row
  * stride ldw elements); q: int8 [V, H] (row stride ldq bytes); scale: fp32 [V].  s = max(max|w|, 1e-8) / 127,

@@ -326,3 +326,30 @@ def combine_head_stats(parts):
     m_star = ls.max(axis=0)
     lse = m_star + np.log(np.exp(ls - m_star[None, :]).sum(axis=0))
     return best.astype(np.float32), arg, lse
+
+
+# ----------------------------------------------------------------------------------------------
+# fused RMSNorm before qkv / gate_up (survey row (f)1; vLLM's RMSNorm, not the reference plugin)
+# ----------------------------------------------------------------------------------------------
+def rms_norm_ref(x_bits, res_bits, gamma_bits, eps: float):
+    """vLLM's RMSNorm on bf16 tensors (vllm/ir/ops/layernorm.py, ``rms_norm`` / ``fused_add_rms_norm``):
+    ``z = float(x) (+ float(residual))``, new residual ``bf16(z)``, ``r = rsqrt(mean(z^2) + eps)`` in fp32,
+    output ``bf16(float(bf16(z * r)) * float(gamma))``.  Returns (normalized bf16 bits [M, K], new residual bits)."""
+    z = bf16_to_f32(x_bits).astype(np.float32)
+    if res_bits is not None:
+        z = (z + bf16_to_f32(res_bits)).astype(np.float32)
+    var = (z.astype(np.float64) ** 2).mean(axis=1, keepdims=True).astype(np.float32)
+    r = (np.float32(1.0) / np.sqrt((var + np.float32(eps)).astype(np.float32))).astype(np.float32)
+    zr = f32_to_bf16((z * r).astype(np.float32))
+    out = f32_to_bf16((bf16_to_f32(zr) * bf16_to_f32(gamma_bits)[None, :]).astype(np.float32))
+    return out, f32_to_bf16(z)
+
+
+def rmsnorm_w8a16_mm(x_bits, res_bits, gamma_bits, eps: float, W, s, silu: bool = False):
+    """The unfused sequence the fused kernel replaces: vLLM's RMSNorm, then the W8A16 GEMM (``w8a16_mm``) on its bf16
+    output, then (``silu``) vLLM's SiluAndMul on the merged gate_up output.  Returns (y bits, new residual bits)."""
+    a, res_out = rms_norm_ref(x_bits, res_bits, gamma_bits, eps)
+    y = w8a16_mm(a, W, s, "bf16")
+    if silu:
+        y = silu_mul(y, W.shape[0] // 2)
+    return y, res_out

@@ -46,6 +46,10 @@ SIGNATURES = [
     ("qf_w8a16_gemm_silu_mul", _c.c_int,
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int, _c.c_int,
       _c.c_int, _c.c_void_p, _c.c_size_t, _c.c_uint, _c.c_void_p]),
+    ("qf_w8a16_gemm_rmsnorm", _c.c_int,
+     [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_float, _c.c_void_p, _c.c_int64, _c.c_void_p,
+      _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_void_p,
+      _c.c_size_t, _c.c_uint, _c.c_void_p]),
     ("qf_w8a8_workspace_bytes", _c.c_size_t, [_c.c_int, _c.c_int]),
     ("qf_w8a8_gemm", _c.c_int,
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int,

@@ -88,7 +88,9 @@ constexpr size_t kWsCtaStats = kWsPartials + sizeof(float) * kPartialSlotFloats 
 constexpr size_t kWsCtaDraws = kWsCtaStats + sizeof(float4) * 16 * kMaxGrid;  // float4 [16 tokens][kMaxGrid CTAs]
 constexpr size_t kWsBytes = kWsCtaDraws + sizeof(float4) * 16 * kMaxGrid;     // head draws, same layout
 
-template <int BN, int NT, int KS> struct Geo {
+constexpr int kNormMaxK = 8192;  // fused RMSNorm: gamma staged in shared memory, K <= this
+
+template <int BN, int NT, int KS, bool NORM = false> struct Geo {
   static constexpr int B = KS / 128;                            // 128-byte weight boxes per stage
   static constexpr int MT = BN / 16;                            // m-tiles per tile (8, 4, 2)
   // m-tiles per consumer warp: 4 where the stage's boxes still split evenly over the four warp pairs, else 2.
@@ -99,13 +101,16 @@ template <int BN, int NT, int KS> struct Geo {
   static constexpr int kWBoxBytes = BN * 128;
   static constexpr int kWBytes = BN * KS;                       // weight bytes per stage
   static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT tokens][64 bf16] (rows >= M stay zero)
-  static constexpr int kXStageBytes = 2 * B * kXBoxBytes;
+  static constexpr int kXBoxesBytes = 2 * B * kXBoxBytes;     // activation boxes of a stage
+  static constexpr int kXStageBytes = (NORM ? 2 : 1) * kXBoxesBytes;  // + the residual's boxes (fused RMSNorm)
+  // fused RMSNorm: gamma [kNormMaxK + 1024] bf16 (zero past K), row scales [16], per-warp partial sums [8][16]
+  static constexpr int kNormBytes = NORM ? (kNormMaxK + 1024) * 2 + 16 * 4 + 8 * 16 * 4 : 0;
   static constexpr int kStageBytes = kWBytes + kXStageBytes;
   static constexpr int kRedBytes = kConsumerWarps * MW * 32 * 4 * NT * 4;  // [warp][m-tile of group][lane][4NT]
   static constexpr int kStatBytes = 8 * 16 * 16;                          // float4 [m-tile][token]
   static constexpr int kOutStride = BN + 8;                               // bf16 [16 tokens][BN + 8] (padded)
   static constexpr int kOutBytes = 16 * kOutStride * 2;
-  static constexpr int kFixedBytes = kRedBytes + kStatBytes + kOutBytes + 2 * 16 * 8 + 64 + 1024;
+  static constexpr int kFixedBytes = kRedBytes + kStatBytes + kOutBytes + 2 * 16 * 8 + 64 + 1024 + kNormBytes;
   static constexpr int kBudget = 226 * 1024;
   static constexpr int kStagesFit = (kBudget - kFixedBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 10 ? 10 : kStagesFit;
@@ -115,13 +120,16 @@ template <int BN, int NT, int KS> struct Geo {
   static constexpr int kOffOut = kOffStat + kStatBytes;
   static constexpr int kOffBar = kOffOut + kOutBytes;         // full[S], empty[S]
   static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;  // abort, last
-  static constexpr int kSmemBytes = kOffFlag + 64 + 1024;     // + alignment slack
+  static constexpr int kOffNorm = kOffFlag + 64;               // fused RMSNorm data
+  static constexpr int kSmemBytes = kOffNorm + kNormBytes + 1024;  // + alignment slack
   static_assert(BPW >= 1 && B * NMW == 4 * BPW && 4 % NMW == 0, "the four warp pairs cover the stage's boxes evenly");
   static_assert(kStages >= 3, "pipeline too shallow");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 struct Params {
+  const __nv_bfloat16* x;  // activations (read directly by the fused RMSNorm prologue)
+  int64_t ldx;
   const float* scale;
   const __nv_bfloat16* bias;
   void* y;
@@ -140,6 +148,14 @@ struct Params {
   uint32_t x_tx;  // activation bytes per stage: 2 B boxes of M rows x 128 bytes
   int out_vec;     // bf16 output rows (y or logits) can be written with 16-byte stores
   int silu_I;      // > 0: gate_up with SiLU(gate) * up fused; the weight holds gate rows [0, I), up rows [I, 2I)
+  // fused RMSNorm of the activations (NORM instances): z = x (+ residual), a = bf16(bf16(z) * gamma) feeds the MMA,
+  // every token's accumulators are scaled by rsqrt(mean(z^2) + eps); bf16(z) is written to res_out
+  const __nv_bfloat16* res;
+  int64_t ldr;
+  const __nv_bfloat16* gamma;
+  __nv_bfloat16* res_out;
+  int64_t ldro;
+  float eps;
   // fused all-reduce of y over the tensor-parallel ranks (row-parallel layers); ar_world == 0: off
   int ar_world, ar_rank, ar_max_count;
   uint8_t* ar_bufs[QF_AR_MAX_RANKS];
@@ -258,6 +274,8 @@ __device__ __forceinline__ void tile_ctas(int tile, const Params& p, int& c_firs
   const int nxt = ((tile + 1) * p.Gsk) / p.r;
   c_last = (tile + 1 < p.r && split_start(nxt, p) <= i1) ? nxt : nxt - 1;
 }
+
+__device__ __forceinline__ int ctid_early() { return static_cast<int>(threadIdx.x); }  // consumer thread 0..255
 
 __device__ __forceinline__ void record_error(uint8_t* ws, int code) {
   atomicExch(reinterpret_cast<int*>(ws), code);
@@ -397,6 +415,21 @@ __device__ __forceinline__ void mma_chunk(float (&acc)[NT][4], const uint4& ra, 
         mma_bf16_m16n8k16(acc[nt], a0, a1, a2, a3, b0, b1);
     }
   }
+}
+
+// Fused RMSNorm, per 8 bf16 columns: a = bf16(bf16(x + r) * g) (z rounded to bf16 as the residual the norm reads,
+// then times gamma, one more rounding); the token's rsqrt(mean z^2 + eps) is applied to its accumulators later.
+__device__ __forceinline__ uint32_t norm_pair(uint32_t x, uint32_t r, uint32_t g) {
+  const __nv_bfloat162 z = __floats2bfloat162_rn(__uint_as_float(x << 16) + __uint_as_float(r << 16),
+                                                 __uint_as_float(x & 0xFFFF0000u) + __uint_as_float(r & 0xFFFF0000u));
+  const uint32_t zw = *reinterpret_cast<const uint32_t*>(&z);
+  const __nv_bfloat162 a = __floats2bfloat162_rn(__uint_as_float(zw << 16) * __uint_as_float(g << 16),
+                                                 __uint_as_float(zw & 0xFFFF0000u) * __uint_as_float(g & 0xFFFF0000u));
+  return *reinterpret_cast<const uint32_t*>(&a);
+}
+__device__ __forceinline__ uint4 norm_words(const uint4& x, const uint4& r, const uint4& g) {
+  return make_uint4(norm_pair(x.x, r.x, g.x), norm_pair(x.y, r.y, g.y), norm_pair(x.z, r.z, g.z),
+                    norm_pair(x.w, r.w, g.w));
 }
 
 // (max, first argmax) of bf16 logits: larger value wins, equal values keep the smaller column.
@@ -866,13 +899,14 @@ __device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTi
   __syncwarp();
 }
 
-template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU>
+template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                 const Params p) {
+                 const __grid_constant__ CUtensorMap tmap_r, const Params p) {
   static_assert(!(HEAD && AR), "the head is vocab-parallel: no all-reduce");
   static_assert(!(SILU && (HEAD || AR)), "the fused gate is for the column-parallel gate_up only");
-  using C = Geo<BN, NT, KS>;
+  static_assert(!(NORM && (HEAD || AR)), "the fused RMSNorm is for the column-parallel qkv and gate_up");
+  using C = Geo<BN, NT, KS, NORM>;
   constexpr int S = C::kStages;
   constexpr int B = C::B;
   constexpr int MT = C::MT;
@@ -900,6 +934,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmap_w);
     prefetch_tensormap(&tmap_x);
+    if (NORM && p.res) prefetch_tensormap(&tmap_r);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kConsumerWarps);  // one arrival per consumer warp
@@ -948,6 +983,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int b = 0; b < 2 * B; ++b)
           tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[i], xi.kk * KS + b * 64, 0, pol_x);
+        if (NORM && p.res) {
+#pragma unroll
+          for (int b = 0; b < 2 * B; ++b)
+            tma_load_2d(xs + C::kXBoxesBytes + b * C::kXBoxBytes, &tmap_r, &full_bar[i], xi.kk * KS + b * 64, 0, pol_x);
+        }
         xi.next(p);
       }
       int issued = npre;
@@ -975,6 +1015,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int b = 0; b < 2 * B; ++b)
           tma_load_2d(xs + b * C::kXBoxBytes, &tmap_x, &full_bar[s], pi.kk * KS + b * 64, 0, pol_x);
+        if (NORM && p.res) {
+#pragma unroll
+          for (int b = 0; b < 2 * B; ++b)
+            tma_load_2d(xs + C::kXBoxesBytes + b * C::kXBoxBytes, &tmap_r, &full_bar[s], pi.kk * KS + b * 64, 0, pol_x);
+        }
         pi.next(p);
         issued = i + 1;
       }
@@ -1204,7 +1249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // zero them once so that those MMA columns compute zeros.  The copies write only rows < M of the same boxes.
     const int zrows = 8 * NT - p.M;
     const int per_box = zrows * 8;  // 16-byte units
-    for (int idx = threadIdx.x; idx < S * 2 * B * per_box; idx += kConsumerThreads) {
+    for (int idx = threadIdx.x; idx < S * (NORM ? 4 : 2) * B * per_box; idx += kConsumerThreads) {
       const int box = idx / per_box;
       const int rem = idx - box * per_box;
       *reinterpret_cast<uint4*>(sX + box * C::kXBoxBytes + (p.M + rem / 8) * 128 + (rem % 8) * 16) =
@@ -1213,6 +1258,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(kBarConsumers, kConsumerThreads);
   }
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
+  float* sRms = reinterpret_cast<float*>(smem + C::kOffNorm + (kNormMaxK + 1024) * 2);  // [16] token row scales
+  if constexpr (NORM) {
+    // Fused RMSNorm prologue: gamma into shared memory (zero past K), every token's rsqrt(mean(z^2) + eps) with
+    // z = x (+ residual) in fp32, and bf16(z) written to res_out, chunks of 8 columns shared out over the CTAs.
+    uint4* sGam = reinterpret_cast<uint4*>(smem + C::kOffNorm);
+    float* sPart = sRms + 16;  // [8 warps][16 tokens]
+    const int kch = p.K / 8;   // K % 8 == 0 (host check)
+    for (int i = ctid_early(); i < (kNormMaxK + 1024) / 8; i += kConsumerThreads)
+      sGam[i] = i < kch ? __ldg(reinterpret_cast<const uint4*>(p.gamma) + i) : make_uint4(0u, 0u, 0u, 0u);
+    float part[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) part[m] = 0.f;
+    for (int i = ctid_early(); i < kch; i += kConsumerThreads) {
+      const bool mine = p.res_out && (i % p.G) == static_cast<int>(blockIdx.x);
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        if (m < p.M) {
+          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx) + i);
+          const uint4 rv = p.res ? __ldg(reinterpret_cast<const uint4*>(p.res + static_cast<int64_t>(m) * p.ldr) + i)
+                                 : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+          const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+          uint32_t zw[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float z0 = __uint_as_float(xw[q] << 16) + __uint_as_float(rw[q] << 16);
+            const float z1 = __uint_as_float(xw[q] & 0xFFFF0000u) + __uint_as_float(rw[q] & 0xFFFF0000u);
+            part[m] = fmaf(z0, z0, part[m]);
+            part[m] = fmaf(z1, z1, part[m]);
+            const __nv_bfloat162 zb = __floats2bfloat162_rn(z0, z1);
+            zw[q] = *reinterpret_cast<const uint32_t*>(&zb);
+          }
+          if (mine)
+            reinterpret_cast<uint4*>(p.res_out + static_cast<int64_t>(m) * p.ldro)[i] = make_uint4(zw[0], zw[1], zw[2], zw[3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      float v = part[m];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) sPart[warp * 16 + m] = v;
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (ctid_early() < 16) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) sum += sPart[w * 16 + ctid_early()];
+      sRms[ctid_early()] = ctid_early() < p.M ? rsqrtf(sum / static_cast<float>(p.K) + p.eps) : 0.f;
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+  }
   // Warp (u, h), u = warp / 2: m-tile group mg = u % NMW (m-tiles MW * mg ..), weight boxes
   // b = u / NMW + j * (4 / NMW), j < BPW.
   const int h = warp & 1;           // which half of each box's 16-byte k chunks
@@ -1263,6 +1361,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         xa[nt] = lds128(xbase + nt * 1024 + x_u0);
         xb[nt] = lds128(xbase + nt * 1024 + x_u1);
       }
+      if constexpr (NORM) {
+        // a = bf16(bf16(x + residual) * gamma) for this lane's 16 k columns of each token row
+        const int k0 = it.kk * KS + 64 * (2 * (b0 + db) + (c >> 2)) + 16 * (c & 3);
+        const uint32_t gbase = smem_u32(smem + C::kOffNorm) + static_cast<uint32_t>(k0 * 2);
+        const uint4 ga = lds128(gbase), gb = lds128(gbase + 16);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          uint4 ra = make_uint4(0u, 0u, 0u, 0u), rb = ra;
+          if (p.res) {
+            ra = lds128(xbase + C::kXBoxesBytes + nt * 1024 + x_u0);
+            rb = lds128(xbase + C::kXBoxesBytes + nt * 1024 + x_u1);
+          }
+          xa[nt] = norm_words(xa[nt], ra, ga);
+          xb[nt] = norm_words(xb[nt], rb, gb);
+        }
+      }
       const uint32_t wbase = sW_u32 + s * C::kWBytes + w_off + db * C::kWBoxBytes;
       uint4 ra[MW], rb[MW];  // m-tile j: rows g and g + 8 of the tile's 16
 #pragma unroll
@@ -1305,13 +1419,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tcount > 0) named_bar_sync(kBarFree, kConsumerThreads + 32);  // the previous tile's sums have been read
     {
       float* mine = sRed + (warp * MW * 32 + lane) * 4 * NT;
+      float rs[NT][2];  // fused RMSNorm: tokens 8 nt + 2 t and 8 nt + 2 t + 1 of this lane's accumulators
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        rs[nt][0] = NORM ? sRms[8 * nt + 2 * t] : 1.f;
+        rs[nt][1] = NORM ? sRms[8 * nt + 2 * t + 1] : 1.f;
+      }
 #pragma unroll
       for (int j = 0; j < MW; ++j)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            mine[j * 32 * 4 * NT + nt * 4 + e] = acc[j][nt][e];
+            mine[j * 32 * 4 * NT + nt * 4 + e] = NORM ? acc[j][nt][e] * rs[nt][e & 1] : acc[j][nt][e];
             acc[j][nt][e] = 0.f;
           }
     }
@@ -1540,11 +1660,11 @@ void pick_tiles(int N, int K, int sms, int* bn, int* ks, int* dp_grid) {
   }
 }
 
-template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU>
+template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU, bool NORM>
 int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
            unsigned flags, cudaStream_t stream) {
-  using C = Geo<BN, NT, KS>;
-  auto kern = w8a16_kernel<BN, NT, KS, HEAD, AR, SILU>;
+  using C = Geo<BN, NT, KS, NORM>;
+  auto kern = w8a16_kernel<BN, NT, KS, HEAD, AR, SILU, NORM>;
   static bool smem_attr_set[64] = {};
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -1563,9 +1683,18 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   rc = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M),
                  xstride, 64, static_cast<uint32_t>(p.M));
   if (rc) return rc;
+  CUtensorMap tr = tx;  // fused RMSNorm: the residual, same shape as x
+  if (NORM && p.res) {
+    const uint64_t rstride = (p.M > 1) ? static_cast<uint64_t>(p.ldr) * 2 : xstride;
+    rc = encode_2d(&tr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.res, static_cast<uint64_t>(p.K),
+                   static_cast<uint64_t>(p.M), rstride, 64, static_cast<uint32_t>(p.M));
+    if (rc) return rc;
+  }
 
   p.f16_path = f16_path();
-  p.x_tx = static_cast<uint32_t>(2 * C::B * p.M * 128);
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = p.M > 1 ? ldx : p.K;
+  p.x_tx = static_cast<uint32_t>((NORM && p.res ? 2 : 1) * 2 * C::B * p.M * 128);
   p.kiters = (p.K + KS - 1) / KS;
   p.ntiles = p.silu_I ? (p.silu_I + BN / 2 - 1) / (BN / 2) : (p.N + BN - 1) / BN;
   if (p.ntiles > kMaxTiles) return fail(QF_ERR_SHAPE, "too many tiles for this tile height");
@@ -1607,16 +1736,19 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (flags & QF_FLAG_PDL) ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, tr, p);
   if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("launch: ") + cudaGetErrorString(e));
   return QF_OK;
 }
 
-template <int BN, int KS, int HEAD, bool AR, bool SILU>
+template <int BN, int KS, int HEAD, bool AR, bool SILU, bool NORM>
 int launch_nt(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
               unsigned flags, cudaStream_t st) {
-  if (p.M <= 8) return launch<BN, 1, KS, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  return launch<BN, 2, KS, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (p.M <= 8) return launch<BN, 1, KS, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  // the fused RMSNorm also stages the residual: with two token tiles the 512- and 1024-byte stages would leave fewer
+  // than three ring stages, so those tile heights run with half the k bytes per stage
+  constexpr int KS2 = (NORM && KS >= 512 && BN * KS >= 32768) ? KS / 2 : KS;
+  return launch<BN, 2, KS2, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
 // Optional fixed tile shape (QF_TILES="BN:KS"; 0 = the per-shape choice): used by the
@@ -1635,18 +1767,18 @@ const TileShape& tile_override() {
   return v;
 }
 
-template <int HEAD, bool AR = false, bool SILU = false>
+template <int HEAD, bool AR = false, bool SILU = false, bool NORM = false>
 int launch_any(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
                unsigned flags, cudaStream_t st) {
   int bn = tile_override().bn, ks = tile_override().ks, dp_grid = 0;
   if (bn == 0) pick_tiles(p.N, p.K, dinfo->sm_count, &bn, &ks, &dp_grid);
   p.G = dp_grid;  // launch() takes it as an upper bound of the grid
-  if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 64 && ks == 512) return launch_nt<64, 512, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 32 && ks == 512) return launch_nt<32, 512, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
-  if (bn == 32 && ks == 1024) return launch_nt<32, 1024, HEAD, AR, SILU>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 128 && ks == 128) return launch_nt<128, 128, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 128 && ks == 256) return launch_nt<128, 256, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 256) return launch_nt<64, 256, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 64 && ks == 512) return launch_nt<64, 512, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 512) return launch_nt<32, 512, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  if (bn == 32 && ks == 1024) return launch_nt<32, 1024, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
   return fail(QF_ERR_SHAPE, "no kernel instance for the chosen tile shape");
 }
 
@@ -1742,6 +1874,67 @@ int qf_w8a16_gemm_silu_mul(const void* x, int64_t ldx, const int8_t* w, int64_t 
   p.ws = static_cast<uint8_t*>(ws);
   p.silu_I = N / 2;
   return launch_any<0, false, true>(x, ldx, w, ldw, p, dinfo, dev, flags, static_cast<cudaStream_t>(stream));
+}
+
+int qf_w8a16_gemm_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, const void* gamma, float eps,
+                          void* residual_out, int64_t ldro, const int8_t* w, int64_t ldw, const float* scale, void* y,
+                          int64_t ldy, int M, int N, int K, int silu_mul, void* ws, size_t ws_bytes, unsigned flags,
+                          void* stream) {
+  int rc = check_common(x, ldx, w, ldw, scale, M, N, K, ws, ws_bytes);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return QF_OK;
+  if (K < 8 || K % 8 || K > kNormMaxK) return fail(QF_ERR_SHAPE, "the fused RMSNorm needs K % 8 == 0 and 8 <= K <= 8192");
+  if (silu_mul && N % 2) return fail(QF_ERR_SHAPE, "N must be even with the fused SiLU gate");
+  if (!y || !gamma) return fail(QF_ERR_INVALID, "null y or gamma");
+  if (!(eps >= 0.f) || !std::isfinite(eps)) return fail(QF_ERR_INVALID, "eps must be finite and >= 0");
+  if (M > 1 && ldy < (silu_mul ? N / 2 : N)) return fail(QF_ERR_STRIDE, "ldy too small");
+  if (reinterpret_cast<uintptr_t>(gamma) % 16) return fail(QF_ERR_ALIGN, "gamma must be 16-byte aligned");
+  if (residual) {
+    if (M > 1 && ldr < K) return fail(QF_ERR_STRIDE, "ldr < K");
+    if (reinterpret_cast<uintptr_t>(residual) % 16 || (M > 1 && ldr % 8))
+      return fail(QF_ERR_ALIGN, "residual must be 16-byte aligned with ldr % 8 == 0");
+  }
+  if (residual_out) {
+    if (M > 1 && ldro < K) return fail(QF_ERR_STRIDE, "ldro < K");
+    if (reinterpret_cast<uintptr_t>(residual_out) % 16 || (M > 1 && ldro % 8))
+      return fail(QF_ERR_ALIGN, "residual_out must be 16-byte aligned with ldro % 8 == 0");
+    // every CTA reads the whole of x and residual: residual_out must not overlap them
+    const uintptr_t o0 = reinterpret_cast<uintptr_t>(residual_out);
+    const uintptr_t o1 = o0 + 2 * (static_cast<uint64_t>(M - 1) * (M > 1 ? ldro : K) + K);
+    const void* ins[2] = {x, residual};
+    const int64_t lds[2] = {ldx, ldr};
+    for (int j = 0; j < 2; ++j) {
+      if (!ins[j]) continue;
+      const uintptr_t i0 = reinterpret_cast<uintptr_t>(ins[j]);
+      const uintptr_t i1 = i0 + 2 * (static_cast<uint64_t>(M - 1) * (M > 1 ? lds[j] : K) + K);
+      if (o0 < i1 && i0 < o1) return fail(QF_ERR_INVALID, "residual_out overlaps x or residual");
+    }
+  }
+  int dev;
+  DeviceInfo* dinfo;
+  rc = device_info(&dev, &dinfo);
+  if (rc) return rc;
+  Params p = {};
+  p.scale = scale;
+  p.y = y;
+  p.ldy = ldy;
+  p.out_vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (M == 1 || ldy % 8 == 0);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ws = static_cast<uint8_t*>(ws);
+  p.res = static_cast<const __nv_bfloat16*>(residual);
+  p.ldr = M > 1 ? ldr : K;
+  p.gamma = static_cast<const __nv_bfloat16*>(gamma);
+  p.res_out = static_cast<__nv_bfloat16*>(residual_out);
+  p.ldro = M > 1 ? ldro : K;
+  p.eps = eps;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (silu_mul) {
+    p.silu_I = N / 2;
+    return launch_any<0, false, true, true>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  }
+  return launch_any<0, false, false, true>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
 int qf_w8a16_gemm_allreduce(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale, void* y,

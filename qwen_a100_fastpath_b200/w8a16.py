@@ -387,3 +387,52 @@ def prefill_workspace_status(device=None, stream=None) -> int:
     st = ctypes.c_int(0)
     check("qf_workspace_status", LIB.qf_workspace_status(buf.data_ptr(), stream.cuda_stream, ctypes.byref(st)))
     return st.value
+
+
+def w8a16_mm_rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float, w_t: torch.Tensor, w_scale: torch.Tensor,
+                     residual: torch.Tensor | None = None, silu_mul: bool = False,
+                     residual_out: torch.Tensor | None = None, want_residual: bool = True, out: torch.Tensor | None = None,
+                     pdl: bool | None = None):
+    """The RMSNorm before qkv / gate_up fused into the W8A16 GEMM (``qf_w8a16_gemm_rmsnorm``): with
+    ``z = x (+ residual)``, returns ``(y, bf16(z))`` where ``y`` is the GEMM of the normalized activations (vLLM's
+    ``RMSNorm(x, residual)`` followed by the linear), ``[M, N]`` bf16, or with ``silu_mul`` the gate_up activation
+    ``[M, N/2]``.  The activation fed to the contraction is ``bf16(bf16(z) * gamma)`` and each token's accumulators
+    are scaled by ``rsqrt(mean(z^2) + eps)``: the same result up to the rounding of the normalized activation."""
+    if x.dim() != 2 or w_t.shape[0] != x.shape[1]:
+        raise ValueError("x must be [M, K] matching w_t [K, N]")
+    M, K = x.shape
+    N = w_t.shape[1]
+    if M > SMALL_M or K < 8 or K % 8 or K > 8192 or (silu_mul and N % 2):
+        raise ValueError(f"need M <= {SMALL_M}, K % 8 == 0, 8 <= K <= 8192 (and an even N with silu_mul)")
+    tensors = [x, w_t, w_scale, gamma] + ([residual] if residual is not None else [])
+    if not all(t.is_cuda for t in tensors) or x.dtype != torch.bfloat16 or gamma.dtype != torch.bfloat16:
+        raise ValueError("libqf_b200 needs CUDA tensors, bf16 activations and a bf16 gamma (there is no CPU path)")
+    if residual is not None and (residual.shape != x.shape or residual.dtype != torch.bfloat16):
+        raise ValueError("residual must be bf16 [M, K]")
+    scale = w_scale.reshape(-1).contiguous()
+    if scale.numel() != N or scale.dtype != torch.float32:
+        raise ValueError("w_scale must hold N fp32 per-channel scales")
+    gamma = gamma.reshape(-1).contiguous()
+    if gamma.numel() != K:
+        raise ValueError("gamma must hold K values")
+    ldw = _check_weight(w_t, K)
+    x = _aligned_rows(x)
+    if residual is not None:
+        residual = _aligned_rows(residual)
+    if want_residual and residual_out is None:
+        residual_out = torch.empty((M, K), dtype=torch.bfloat16, device=x.device)
+    n_out = N // 2 if silu_mul else N
+    if out is None:
+        out = torch.empty((M, n_out), dtype=torch.bfloat16, device=x.device)
+    stream = torch.cuda.current_stream(x.device)
+    ws = workspace(x.device, stream, LIB.qf_w8a16_workspace_bytes(M, N, K))
+    flags = _lib.QF_FLAG_PDL if (_PDL_DEFAULT if pdl is None else pdl) else 0
+    rc = LIB.qf_w8a16_gemm_rmsnorm(
+        x.data_ptr(), x.stride(0), residual.data_ptr() if residual is not None else None,
+        residual.stride(0) if residual is not None else K, gamma.data_ptr(), float(eps),
+        residual_out.data_ptr() if residual_out is not None else None,
+        residual_out.stride(0) if residual_out is not None else K, w_t.data_ptr(), ldw, scale.data_ptr(),
+        out.data_ptr(), out.stride(0), M, N, K, 1 if silu_mul else 0, ws.data_ptr(), ws.numel(), flags,
+        stream.cuda_stream)
+    check("qf_w8a16_gemm_rmsnorm", rc)
+    return out, residual_out
