@@ -5,8 +5,9 @@ function in tests/test_oracle_golden.py), then the W8A16 GEMM contract, then (ga
 Bars: the new residual bf16(x + residual) is bit-identical; the GEMM output, whose only difference from the unfused
 sequence is the rounding of the normalized activation (the fused kernel rounds bf16(z) * gamma once and scales the
 fp32 accumulators by rsqrt(mean z^2 + eps); vLLM rounds z * r and then times gamma), is within the north-star bound
-(max abs error <= 2e-2 * max|y|) and within 5e-3 relative in Frobenius norm; also against the library's own unfused
-pair (the oracle's normalized activations through qf_w8a16_gemm).
+(max abs error <= 2e-2 * max|y|) and within 5e-3 relative in Frobenius norm (1e-2 with the SiLU gate, whose product
+silu(g) * u carries the rounding difference of both g and u); also against the library's own unfused pair (the
+oracle's normalized activations through qf_w8a16_gemm).
 """
 from __future__ import annotations
 
@@ -58,7 +59,7 @@ def test_fused_rmsnorm_gemm(dev, M, N, K, silu, with_res):
     torch.cuda.synchronize()
     y_ref, res_ref = orc.rmsnorm_w8a16_mm(x, res, gamma, eps, W, s, silu=silu)
     assert np.array_equal(from_dev_bf16(res_out), res_ref)
-    close(from_dev_bf16(y), y_ref)
+    close(from_dev_bf16(y), y_ref, frob=1e-2 if silu else 5e-3)
     if not silu:  # against the library's own unfused pair: oracle norm, then the GEMM kernel
         a_ref, _ = orc.rms_norm_ref(x, res, gamma, eps)
         y2 = w8a16_mm(to_dev_bf16(a_ref, dev), wt, st, None, torch.bfloat16)
