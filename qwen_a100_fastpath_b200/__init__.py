@@ -27,5 +27,6 @@ def register():
         logger.info("qwen_fastpath: QWEN_FAST_ATTN is not provided by the B200 build; FlashAttention stays")
     if os.environ.get("QWEN_FAST_LINEAR", "1") == "1":
         patches.patch_int8_linear()
+        patches.patch_row_parallel()
     if os.environ.get("QWEN_FAST_DRAFT_HEAD", "1") == "1":
         patches.patch_draft_lm_head()

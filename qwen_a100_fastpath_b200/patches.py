@@ -123,18 +123,24 @@ def quantize_head_rows(weight: torch.Tensor, block_rows: int = 16384):
 
 
 def attach_int8_head(draft_model) -> bool:
-    """Give a draft model (``Qwen3_5MTP``-like: ``lm_head.weight`` 2-D, ``lm_head.tp_size == 1``) its int8
-    head copy (patches.py:133-152).  Returns True if attached."""
+    """Give a draft model (``Qwen3_5MTP``-like: ``lm_head.weight`` 2-D) its int8 head copy (patches.py:133-152).
+    The reference requires ``lm_head.tp_size == 1`` (patches.py:138); here a vocab-sharded head (tensor parallel) is
+    taken too: each rank quantizes its own shard (the quantizer is per row), its statistics are combined over the
+    ranks in ``get_top_tokens`` and its logits gathered as vLLM's LogitsProcessor does in ``compute_logits``.  Heads
+    with added (LoRA) vocabulary keep the original path.  Returns True if attached."""
     lm_head = getattr(draft_model, "lm_head", None)
     weight = getattr(lm_head, "weight", None)
-    if weight is None or weight.dim() != 2 or getattr(lm_head, "tp_size", 1) != 1:
+    si = getattr(lm_head, "shard_indices", None)
+    if weight is None or weight.dim() != 2 or si is None or getattr(si, "num_added_elements", 0):
         return False
     from .w8a16 import pick_config
     V, H = weight.shape
     w8, scale = quantize_head_rows(weight)
-    num_pad = lm_head.shard_indices.num_org_vocab_padding
+    num_pad = si.num_org_vocab_padding
     draft_model._qf_head_i8 = (w8.t(), scale, num_pad, pick_config(V, H))
-    logger.info("qwen_fastpath: int8 draft lm_head (%d x %d, %.2f GB) for MTP proposals", V, H, w8.numel() / 1e9)
+    draft_model._qf_head_tp = int(getattr(lm_head, "tp_size", 1))
+    logger.info("qwen_fastpath: int8 draft lm_head (%d x %d, %.2f GB, tp %d) for MTP proposals", V, H,
+                w8.numel() / 1e9, draft_model._qf_head_tp)
     return True
 
 
@@ -157,6 +163,11 @@ def int8_head(model, hidden_states: torch.Tensor, want_logits: bool = True):
     V = w_t.shape[1]
     out = w8a16_head(hidden_states, w_t, scale, n_valid=V - num_pad, vocab_offset=si.org_vocab_start_index,
                      want_logits=want_logits, pdl=True)
+    if model.__dict__.get("_qf_head_tp", 1) > 1:
+        # vocab shards: combine the per-shard (max, argmax, lse) over the tensor-parallel ranks (collective: every
+        # rank takes this path with the same shapes)
+        from .tp import gather_head_stats
+        out = (out[0], *gather_head_stats(out[1], out[2], out[3], group=_tp_group().device_group))
     model._qf_head_stats = out[1:]
     return out
 
@@ -167,7 +178,12 @@ def draft_compute_logits(model, hidden_states: torch.Tensor, spec_step_idx, orig
     out = int8_head(model, hidden_states)
     if out is None:
         return orig_logits(model, hidden_states, spec_step_idx)
-    return out[0][..., : model.logits_processor.org_vocab_size]
+    logits = out[0]
+    if model.__dict__.get("_qf_head_tp", 1) > 1:  # vocab shards: gather them as vLLM's LogitsProcessor does
+        logits = model.logits_processor._gather_logits(logits)
+        if logits is None:  # ranks other than 0 under a gather (not all-gather)
+            return None
+    return logits[..., : model.logits_processor.org_vocab_size]
 
 
 def draft_get_top_tokens(model, hidden_states: torch.Tensor, orig_logits, orig_top=None):
@@ -184,6 +200,95 @@ def draft_get_top_tokens(model, hidden_states: torch.Tensor, orig_logits, orig_t
     if si.num_org_vocab_padding > 0:
         logits[..., -si.num_org_vocab_padding:] = -float("inf")
     return logits.argmax(dim=-1) + si.org_vocab_start_index
+
+
+# ----------------------------------------------------------------------------------------------
+# tensor parallelism: row-parallel linears with the all-reduce fused into the GEMM
+# ----------------------------------------------------------------------------------------------
+def _tp_group():
+    """vLLM's tensor-parallel GroupCoordinator (``cpu_group`` for the buffer exchange, ``device_group`` for the
+    small gathers)."""
+    from vllm.distributed import get_tp_group
+    return get_tp_group()
+
+
+_ROW_COMMS: dict = {}
+
+
+def _make_row_comm(group, max_count: int):
+    from .tp import NVLinkAllReduce
+    return NVLinkAllReduce(max_count, group=group.cpu_group)
+
+
+def row_comm(group, count: int):
+    """The NVLink buffers of this process's tensor-parallel group, made on first use (collective: the ranks run the
+    same layers in the same order).  None while a CUDA graph is being captured and no buffers exist yet (the IPC
+    exchange cannot be captured); the layer then keeps vLLM's path for that call on every rank."""
+    key = (torch.cuda.current_device(), id(group))
+    comm = _ROW_COMMS.get(key)
+    if comm is None or comm.max_count < count:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        comm = _make_row_comm(group, max(count, 16 * 8192))
+        _ROW_COMMS[key] = comm
+    return comm
+
+
+def row_parallel_forward(layer, input_: torch.Tensor):
+    """Body of the patched ``RowParallelLinear.forward`` for a W8A8-int8 layer under tensor parallelism whose
+    output is reduced (o_proj, down): this rank's K-shard GEMM with the all-reduce in its epilogue over NVLink
+    (``qf_w8a16_gemm_allreduce``; vLLM would run the shard GEMM and then ``tensor_model_parallel_all_reduce``).
+    Returns None where it does not apply (the caller then runs vLLM's forward): no reduction, one rank, another
+    quant kernel or static activation scales, more than 16 rows, non-bf16 activations, a weight view the tensor maps
+    cannot take.  The bias is added once after the sum (vLLM adds it on rank 0 before the sum: the same value up
+    to the bf16 rounding of the partial)."""
+    from .w8a16 import SMALL_M, w8a16_mm_allreduce
+    if not getattr(layer, "reduce_results", False) or getattr(layer, "tp_size", 1) <= 1:
+        return None
+    kernel = getattr(getattr(layer, "scheme", None), "kernel", None)
+    if kernel is None or not getattr(getattr(type(kernel), "apply_weights", None), "_qwen_fastpath", False):
+        return None
+    w_q, w_s, i_s, i_zp, azp_adj = kernel._get_layer_params(layer)
+    if i_s is not None or i_zp is not None or azp_adj is not None:
+        return None
+    if layer.input_is_parallel:
+        x = input_
+    else:
+        x = input_.chunk(layer.tp_size, dim=-1)[layer.tp_rank].contiguous()
+    K = x.shape[-1]
+    N = w_q.shape[1]
+    M = x.numel() // K if K else 0
+    if (x.dtype is not torch.bfloat16 or not 1 <= M <= SMALL_M or w_q.stride(0) != 1 or w_s.numel() != N
+            or w_q.data_ptr() % 16 or (N > 1 and w_q.stride(1) % 16)):
+        return None
+    comm = row_comm(_tp_group(), M * ((N + 127) // 128 * 128))
+    if comm is None:
+        return None
+    y = w8a16_mm_allreduce(x.reshape(M, K), w_q, w_s, comm, pdl=True).view(*x.shape[:-1], N)
+    bias = getattr(layer, "bias", None)
+    if bias is not None and not layer.skip_bias_add:
+        y = y + bias
+    if not getattr(layer, "return_bias", False):
+        return y
+    return y, (bias if layer.skip_bias_add else None)
+
+
+def patch_row_parallel() -> bool:
+    """Route reduced row-parallel int8 layers through the fused GEMM + NVLink all-reduce under tensor parallelism."""
+    from vllm.model_executor.layers.linear import RowParallelLinear
+    orig = RowParallelLinear.forward
+    if getattr(orig, "_qwen_fastpath", False):
+        return False
+
+    def forward(self, input_):
+        out = row_parallel_forward(self, input_)
+        return orig(self, input_) if out is None else out
+
+    forward._qwen_fastpath = True
+    forward._qf_orig = orig
+    RowParallelLinear.forward = forward
+    logger.info("qwen_fastpath: row-parallel int8 linears (M <= 16) with the all-reduce fused over NVLink")
+    return True
 
 
 def patch_draft_lm_head() -> bool:

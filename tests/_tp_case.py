@@ -2,8 +2,8 @@
 NVLinkAllReduce (qf_allreduce_bf16) against the fp32 rank-order sum of every rank's input, eager and inside a
 CUDA graph, for the decode sizes M x 5120 (M = 1, 5, 16); and the row-parallel GEMM with the fused all-reduce
 (qf_w8a16_gemm_allreduce) against the rank-order sum of every rank's partial computed by the plain GEMM kernel
-(the same accumulation, so the comparison is bit-exact).  Exits non-zero on a mismatch.  Used by
-test_gpu_tp.py."""
+(the same accumulation, so the comparison is bit-exact); with two ranks also the plugin's patched RowParallelLinear
+body (patches.row_parallel_forward) with its own buffers.  Exits non-zero on a mismatch.  Used by test_gpu_tp.py."""
 from __future__ import annotations
 
 import os
@@ -82,6 +82,47 @@ def fused_cases(ar, rank: int, world: int, dev, stream) -> int:
     return bad
 
 
+def plugin_row_case(rank: int, world: int, dev) -> int:
+    """The plugin's patched RowParallelLinear body (patches.row_parallel_forward) on a stand-in layer holding this
+    rank's K-shard of an int8 weight: its own NVLink buffers (made by patches.row_comm over the default group) and the
+    fused GEMM + all-reduce, against the rank-order sum of every shard's plain-GEMM partial plus the bias."""
+    import types
+    from qwen_a100_fastpath_b200 import patches
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_mm
+    patches._tp_group = lambda: types.SimpleNamespace(cpu_group=None, device_group=None)
+
+    class Kernel:
+        def apply_weights(self, layer, x, bias=None):
+            raise AssertionError("the fused path replaces apply_weights + all-reduce")
+        apply_weights._qwen_fastpath = True
+
+        def _get_layer_params(self, layer):
+            return layer.w_q, layer.w_s, None, None, None
+
+    bad = 0
+    N = 5120
+    scale = torch.rand(N, device=dev, generator=torch.Generator(device=dev).manual_seed(19)) * 0.009 + 0.001
+    bias = (torch.randn(N, device=dev, generator=torch.Generator(device=dev).manual_seed(20)) * 0.5).to(torch.bfloat16)
+    for (K, M) in [(2176, 5), (4352, 16)]:
+        shards = [shard(5000 + K + M + r, M, N, K, dev) for r in range(world)]
+        x, w = shards[rank]
+        layer = types.SimpleNamespace(reduce_results=True, tp_size=world, tp_rank=rank, input_is_parallel=True,
+                                      bias=bias, skip_bias_add=False, return_bias=False,
+                                      scheme=types.SimpleNamespace(kernel=Kernel()), w_q=w.t(), w_s=scale.view(N, 1))
+        y = patches.row_parallel_forward(layer, x.view(1, M, K))
+        want = reference([w8a16_mm(xr, wr.t(), scale, None, torch.bfloat16) for xr, wr in shards]) + bias
+        torch.cuda.synchronize()
+        if y is None or y.shape != (1, M, N) or not torch.equal(y.view(M, N), want):
+            bad += 1
+            print(f"rank {rank}: plugin row-parallel mismatch K={K} M={M}", flush=True)
+    for comm in patches._ROW_COMMS.values():
+        if comm.status() != 0:
+            bad += 1
+        comm.close()
+    patches._ROW_COMMS.clear()
+    return bad
+
+
 def main() -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -133,6 +174,8 @@ def main() -> int:
             print(f"rank {rank}: graph mismatch rep={rep}", flush=True)
     del graph
     bad += fused_cases(ar, rank, world, dev, stream)
+    if world > 1:
+        bad += plugin_row_case(rank, world, dev)
     status = ar.status()
     if status != 0:
         bad += 1

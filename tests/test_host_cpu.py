@@ -53,7 +53,11 @@ def test_attach_int8_head_and_gates():
     assert patches.attach_int8_head(m)
     w_t, scale, num_pad, cfg = m._qf_head_i8
     assert w_t.shape == (128, 512) and w_t.stride() == (1, 128) and num_pad == 12 and cfg is not None
-    assert not patches.attach_int8_head(fake_model(tp_size=2))       # the reference requires tp_size == 1
+    m2 = fake_model(tp_size=2)                                         # a vocab shard: accepted (the reference is
+    assert patches.attach_int8_head(m2) and m2._qf_head_tp == 2       # tp_size == 1 only, patches.py:138)
+    m3 = fake_model()
+    m3.lm_head.shard_indices.num_added_elements = 8                    # added (LoRA) vocabulary: original path
+    assert not patches.attach_int8_head(m3)
     h = torch.zeros(3, 128, dtype=torch.bfloat16)
     assert patches.int8_head(m, h.float()) is None                     # dtype gate
     assert patches.int8_head(m, torch.zeros(17, 128, dtype=torch.bfloat16)) is None   # M > 16
@@ -81,6 +85,8 @@ def test_register_patches_installed_vllm(monkeypatch):
     from qwen_a100_fastpath_b200 import patches
     cls = vllm_cutlass.CutlassInt8ScaledMMLinearKernel
     orig = cls.apply_weights
+    from vllm.model_executor.layers.linear import RowParallelLinear
+    orig_row = RowParallelLinear.forward
     try:
         monkeypatch.setenv("QWEN_FAST_LINEAR", "1")
         monkeypatch.setenv("QWEN_FAST_DRAFT_HEAD", "1")
@@ -98,8 +104,11 @@ def test_register_patches_installed_vllm(monkeypatch):
         assert y.shape == (2, 3, 640)
         from vllm.model_executor.models import qwen3_5_mtp
         assert getattr(qwen3_5_mtp.Qwen3_5MTP.compute_logits, "_qwen_fastpath", False)
+        assert getattr(RowParallelLinear.forward, "_qwen_fastpath", False)
+        assert patches.patch_row_parallel() is False                     # idempotent
     finally:
         cls.apply_weights = getattr(cls.apply_weights, "_qf_orig", orig)
+        RowParallelLinear.forward = orig_row
 
 
 def test_switches_off(monkeypatch):
@@ -107,6 +116,7 @@ def test_switches_off(monkeypatch):
     from qwen_a100_fastpath_b200 import patches
     called = []
     monkeypatch.setattr(patches, "patch_int8_linear", lambda: called.append("linear"))
+    monkeypatch.setattr(patches, "patch_row_parallel", lambda: called.append("row"))
     monkeypatch.setattr(patches, "patch_draft_lm_head", lambda: called.append("head"))
     monkeypatch.setattr(plugin, "_registered", False)
     monkeypatch.setenv("QWEN_FAST_LINEAR", "0")
@@ -117,4 +127,4 @@ def test_switches_off(monkeypatch):
     monkeypatch.setenv("QWEN_FAST_LINEAR", "1")
     monkeypatch.setenv("QWEN_FAST_DRAFT_HEAD", "0")
     plugin.register()
-    assert called == ["head", "linear"]
+    assert called == ["head", "linear", "row"]
