@@ -67,6 +67,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
     ap.add_argument("--sweep-out", default="")
+    ap.add_argument("--ref-triton", action="store_true", help="with --sweep: also time the reference's own Triton "
+                    "kernel (w8a16_mm with its pick_config, from the reference installed in baseline/_ref)")
     ap.add_argument("--prefill-sweep", action="store_true", help="the M > 16 int8 path (qf_w8a8_gemm: per-token "
                     "quantization + tcgen05 GEMM) on every config-2 GEMM at M = 32..4096, beside torch._int_mm")
     ap.add_argument("--fused-sweep", action="store_true", help="RMSNorm fused into qkv and RMSNorm + SiLU fused into "
@@ -520,11 +522,28 @@ def run_ours(args, rank: int, world: int, local: int):
     print(json.dumps(line), flush=True)
 
 
+def load_reference_triton():
+    """The reference plugin's Triton kernel module (plugin/qwen_fastpath/w8a16.py), installed into baseline/_ref by
+    ``pip install --no-deps --target baseline/_ref <reference>/plugin``; None if it is not installed."""
+    ref_dir = REPO / "baseline" / "_ref"
+    if not (ref_dir / "qwen_fastpath" / "w8a16.py").exists():
+        return None
+    sys.path.insert(0, str(ref_dir))
+    import qwen_fastpath.w8a16 as ref
+    return ref
+
+
 def run_sweep(args, local: int):
     """Config 4: every config-2 GEMM and the head at M in {1,2,3,4,5,8,12,16}, timed alone (CUDA graph of 64
-    launches over distinct weights, so every launch streams from HBM)."""
+    launches over distinct weights, so every launch streams from HBM).  With --ref-triton, the reference's own Triton
+    kernel on the same launches (its w8a16_mm with pick_config; for the head its int8 logits followed by the
+    masked argmax of get_top_tokens, plugin/qwen_fastpath/patches.py:157-185)."""
     import torch
     from qwen_a100_fastpath_b200.w8a16 import w8a16_head, w8a16_head_sample, w8a16_mm
+    ref = load_reference_triton() if args.ref_triton else None
+    if ref is not None:
+        import triton
+        print(json.dumps({"reference_triton": triton.__version__, "module": ref.__file__}), flush=True)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peak, _ = peak_hbm()
@@ -564,8 +583,32 @@ def run_sweep(args, local: int):
             gbs = b / (ms * 1e-3) / 1e9
             rows.append({"gemm": name, "N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "GBps": round(gbs, 1),
                          "frac_measured": round(gbs / peak, 4), "frac_nominal": round(gbs / NOMINAL_HBM_GBS, 4)})
-            print(json.dumps(rows[-1]), flush=True)
             del gr
+            if ref is not None and name != "lm_head_sample":
+                cfg = ref.pick_config(N, K)
+
+                def ref_call(i):
+                    lg = ref.w8a16_mm(x, Ws[i].t(), Ss[i], cfg, torch.bfloat16)
+                    if head:  # get_top_tokens: the argmax over the logits (no padding here)
+                        lg.argmax(dim=-1)
+
+                try:
+                    with torch.cuda.stream(stream):
+                        for i in range(copies):
+                            ref_call(i)
+                    torch.cuda.synchronize()
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=stream):
+                        for i in range(reps):
+                            ref_call(i % copies)
+                    rms = time_graph(gr, stream, 5, 2) / reps
+                    rows[-1]["ref_triton_us"] = round(rms * 1e3, 2)
+                    rows[-1]["ref_triton_GBps"] = round(b / (rms * 1e-3) / 1e9, 1)
+                    rows[-1]["ref_triton_cfg"] = list(cfg) if cfg else None
+                except Exception as e:  # noqa: BLE001 -- the reference kernel may not compile for this GPU
+                    rows[-1]["ref_triton_us"] = None
+                    rows[-1]["ref_triton_error"] = f"{type(e).__name__}: {str(e)[:160]}"
+            print(json.dumps(rows[-1]), flush=True)
         del Ws, Ss
         torch.cuda.empty_cache()
     if args.sweep_out:
