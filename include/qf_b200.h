@@ -118,7 +118,7 @@ int qf_w8a16_head_sample(const void* x, int64_t ldx, const int8_t* w, int64_t ld
  * GPU (different streams) race: order them on one stream.  A device-side timeout is kept in the array until
  * qf_w8a16_noalloc_status reads it. */
 #define QF_NOALLOC_MAX_N 262144
-#define QF_NOALLOC_SCRATCH_BYTES 2655232u
+#define QF_NOALLOC_SCRATCH_BYTES 2675712u
 int qf_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* scale,
                           const void* bias, void* y, int64_t ldy, int y_dtype, int M, int N, int K,
                           unsigned flags, void* stream);
@@ -158,7 +158,8 @@ int qf_w8a8_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const
  * and each token's fp32 accumulators are multiplied by rsqrt(mean(z^2) + eps) (z in fp32) before the scale and the
  * bf16 rounding: the per-token factor commutes with the k-sum, so only the rounding of the normalized activation
  * differs from the unfused sequence.  residual: bf16 [M, K] (ldr) or NULL (z = x); gamma: bf16 [K], 16-byte
- * aligned; residual_out: bf16 [M, K] (ldro) receiving bf16(z), or NULL; it must not overlap x or residual.
+ * aligned; residual_out: bf16 [M, K] (ldro) receiving bf16(z), or NULL; it must not overlap x or residual.  The
+ * sums of z^2 come from the activation stages the kernel streams anyway (no extra pass over x).
  * silu_mul = 0: y = the GEMM output [M, N]; 1: w is the merged gate_up weight and y = bf16(bf16(silu(g)) * u)
  * [M, N/2] as qf_w8a16_gemm_silu_mul.  No bias.  K % 8 == 0, K <= 8192; other arguments as qf_w8a16_gemm. */
 int qf_w8a16_gemm_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, const void* gamma, float eps,

@@ -83,7 +83,8 @@ constexpr size_t kWsHeader = 256;                              // [0] error flag
 constexpr size_t kWsCounters = kWsHeader;                       // int32[kMaxTiles]
 constexpr size_t kWsZeroBytes = kWsCounters + sizeof(int) * kMaxTiles;
 constexpr size_t kWsPartials = (kWsZeroBytes + 1023) / 1024 * 1024;
-constexpr size_t kPartialSlotFloats = kMaxBN * 16;              // [BN rows][8*NT tokens]
+constexpr size_t kSlotSsq = kMaxBN * 16;                         // fused RMSNorm: per-token sum of z^2 [16]
+constexpr size_t kPartialSlotFloats = kSlotSsq + 16;             // [BN rows][8*NT tokens], then the sums
 constexpr size_t kWsCtaStats = kWsPartials + sizeof(float) * kPartialSlotFloats * 2 * kMaxGrid;  // head
 constexpr size_t kWsCtaDraws = kWsCtaStats + sizeof(float4) * 16 * kMaxGrid;  // float4 [16 tokens][kMaxGrid CTAs]
 constexpr size_t kWsBytes = kWsCtaDraws + sizeof(float4) * 16 * kMaxGrid;     // head draws, same layout
@@ -103,8 +104,9 @@ template <int BN, int NT, int KS, bool NORM = false> struct Geo {
   static constexpr int kXBoxBytes = 8 * NT * 128;               // [8*NT tokens][64 bf16] (rows >= M stay zero)
   static constexpr int kXBoxesBytes = 2 * B * kXBoxBytes;     // activation boxes of a stage
   static constexpr int kXStageBytes = (NORM ? 2 : 1) * kXBoxesBytes;  // + the residual's boxes (fused RMSNorm)
-  // fused RMSNorm: gamma [kNormMaxK + 1024] bf16 (zero past K), row scales [16], per-warp partial sums [8][16]
-  static constexpr int kNormBytes = NORM ? (kNormMaxK + 1024) * 2 + 16 * 4 + 8 * 16 * 4 : 0;
+  // fused RMSNorm: gamma [kNormMaxK + 1024] bf16 (zero past K), then the consumer warps' per-token sums of z^2 of
+  // the tile just handed off [8 warps][16 tokens]
+  static constexpr int kNormBytes = NORM ? (kNormMaxK + 1024) * 2 + 8 * 16 * 4 : 0;
   static constexpr int kStageBytes = kWBytes + kXStageBytes;
   static constexpr int kRedBytes = kConsumerWarps * MW * 32 * 4 * NT * 4;  // [warp][m-tile of group][lane][4NT]
   static constexpr int kStatBytes = 8 * 16 * 16;                          // float4 [m-tile][token]
@@ -419,17 +421,25 @@ __device__ __forceinline__ void mma_chunk(float (&acc)[NT][4], const uint4& ra, 
 
 // Fused RMSNorm, per 8 bf16 columns: a = bf16(bf16(x + r) * g) (z rounded to bf16 as the residual the norm reads,
 // then times gamma, one more rounding); the token's rsqrt(mean z^2 + eps) is applied to its accumulators later.
-__device__ __forceinline__ uint32_t norm_pair(uint32_t x, uint32_t r, uint32_t g) {
-  const __nv_bfloat162 z = __floats2bfloat162_rn(__uint_as_float(x << 16) + __uint_as_float(r << 16),
-                                                 __uint_as_float(x & 0xFFFF0000u) + __uint_as_float(r & 0xFFFF0000u));
-  const uint32_t zw = *reinterpret_cast<const uint32_t*>(&z);
+// ss accumulates z^2 (z in fp32, before rounding); zw receives bf16(z) (the new residual).
+__device__ __forceinline__ uint32_t norm_pair(uint32_t x, uint32_t r, uint32_t g, float& ss, uint32_t& zw) {
+  const float z0 = __uint_as_float(x << 16) + __uint_as_float(r << 16);
+  const float z1 = __uint_as_float(x & 0xFFFF0000u) + __uint_as_float(r & 0xFFFF0000u);
+  ss = fmaf(z0, z0, ss);
+  ss = fmaf(z1, z1, ss);
+  const __nv_bfloat162 z = __floats2bfloat162_rn(z0, z1);
+  zw = *reinterpret_cast<const uint32_t*>(&z);
   const __nv_bfloat162 a = __floats2bfloat162_rn(__uint_as_float(zw << 16) * __uint_as_float(g << 16),
                                                  __uint_as_float(zw & 0xFFFF0000u) * __uint_as_float(g & 0xFFFF0000u));
   return *reinterpret_cast<const uint32_t*>(&a);
 }
-__device__ __forceinline__ uint4 norm_words(const uint4& x, const uint4& r, const uint4& g) {
-  return make_uint4(norm_pair(x.x, r.x, g.x), norm_pair(x.y, r.y, g.y), norm_pair(x.z, r.z, g.z),
-                    norm_pair(x.w, r.w, g.w));
+__device__ __forceinline__ uint4 norm_words(const uint4& x, const uint4& r, const uint4& g, float& ss, uint4& z) {
+  return make_uint4(norm_pair(x.x, r.x, g.x, ss, z.x), norm_pair(x.y, r.y, g.y, ss, z.y),
+                    norm_pair(x.z, r.z, g.z, ss, z.z), norm_pair(x.w, r.w, g.w, ss, z.w));
+}
+// rsqrt(mean z^2 + eps) from a token's sum of squares over the K columns.
+__device__ __forceinline__ float norm_factor(const Params& p, float ss) {
+  return rsqrtf(ss / static_cast<float>(p.K) + p.eps);
 }
 
 // (max, first argmax) of bf16 logits: larger value wins, equal values keep the smaller column.
@@ -500,10 +510,22 @@ __device__ __forceinline__ void ar_publish_reduce(const Params& p, int tile, int
 // Reduction of a stream-K tile from every contributor's slot (CTAs c_first .. c_last, in that order), by the
 // contributor that arrived last when the tile's designated reducer did not wait for the others: finishes the tile
 // (scale + store, or logits + tile statistics for the head) and re-arms the tile's counter.
-template <int BN, int NT, int HEAD, bool AR, bool SILU>
+template <int BN, int NT, int HEAD, bool AR, bool SILU, bool NORM>
 __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int lane, int c_first, int c_last,
                                                  int* counters, const float* partials, float4* sTile,
                                                  __nv_bfloat16* sOut, uint32_t ar_epoch, uint64_t ar_bound) {
+  // fused RMSNorm: token `lane` (< 16) sums the contributors' sums of squares (CTA order) into its factor
+  float rfac = 1.f;
+  if constexpr (NORM) {
+    float ss = 0.f;
+    if (lane < 16) {
+      for (int cc = c_first; cc <= c_last; ++cc) {
+        const int ft = split_start(cc, p) / p.kiters;
+        ss += __ldcg(partials + static_cast<size_t>(2 * cc + (tile == ft ? 0 : 1)) * kPartialSlotFloats + kSlotSsq + lane);
+      }
+      rfac = norm_factor(p, ss);
+    }
+  }
   // Slot = [BN rows][8*NT tokens] fp32, read as float4: lane takes float4 f = lane + 32 j (row f / (2 NT),
   // tokens 4 (lane % (2 NT)) + 0..3).  All of a contributor's loads (and those of U contributors) are issued
   // before they are added, in ascending CTA order.
@@ -550,7 +572,11 @@ __device__ __forceinline__ void split_reduce_all(const Params& p, int tile, int 
       const int wr = weight_row<BN, SILU>(p, tile, row);
       const int n = wr < 0 ? p.N : wr;  // past the end: masked below
       const float sc = wr >= 0 ? __ldg(p.scale + wr) : 0.f;
-      const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      if constexpr (NORM) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) vv[e] *= __shfl_sync(0xffffffffu, rfac, m_base + e);
+      }
       uint4 wd = make_uint4(0u, 0u, 0u, 0u);  // head with sampling: noise words of (row, tokens m_base ..)
       if (HEAD == 2 && n < p.n_valid) wd = draw_words(p, n + p.vocab_offset, m_base / 4);
 #pragma unroll
@@ -822,16 +848,32 @@ __device__ __forceinline__ RowScale load_row_scale(const Params& p, int tile, in
 // sums in sRed -- starting from the stream-K peers' sums in sPeer when `peers` -- in the epilogue warp's order, so the
 // bits are the same as finish_tile's, then all consumers store the staged rows.  `rs` holds the m-tile's scales and
 // bias (load_row_scale).  Plain GEMM instances with bf16 output only.
-template <int BN, int NT, int MW, int NMW>
+template <int BN, int NT, int MW, int NMW, bool NORM>
 __device__ __forceinline__ void coop_finish_tile(const Params& p, int tile, int warp, const float* sRed,
                                                  const float* sPeer, bool peers, __nv_bfloat16* sOut,
-                                                 const RowScale& rs) {
+                                                 const RowScale& rs, const float* sSsq) {
   constexpr int MT = BN / 16;
   constexpr int OS = BN + 8;
   static_assert(MT <= kConsumerWarps, "one m-tile per consumer warp");
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2;
   const int t = lane & 3;
+  // fused RMSNorm: this lane's tokens 8 nt + 2 t + bq, from the consumer warps' sums of squares (and the stream-K
+  // peers', staged after their partial sums)
+  float rtk[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int bq = 0; bq < 2; ++bq) {
+      rtk[nt][bq] = 1.f;
+      if constexpr (NORM) {
+        const int m = 8 * nt + 2 * t + bq;
+        float ss = peers ? sPeer[MT * 32 * 4 * NT + m] : 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) ss += sSsq[w * 16 + m];
+        rtk[nt][bq] = norm_factor(p, ss);
+      }
+    }
   if (warp < MT) {
     const int mt = warp;
     float v[NT][4];
@@ -855,8 +897,8 @@ __device__ __forceinline__ void coop_finish_tile(const Params& p, int tile, int 
 #pragma unroll
       for (int bq = 0; bq < 2; ++bq) {
         const int m = 8 * nt + 2 * t + bq;
-        __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][bq] * rs.s0);
-        __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + bq] * rs.s1);
+        __nv_bfloat16 r0 = __float2bfloat16_rn(v[nt][bq] * rtk[nt][bq] * rs.s0);
+        __nv_bfloat16 r1 = __float2bfloat16_rn(v[nt][2 + bq] * rtk[nt][bq] * rs.s1);
         if (p.bias) {
           r0 = __float2bfloat16_rn(__bfloat162float(r0) + rs.b0);
           r1 = __float2bfloat16_rn(__bfloat162float(r1) + rs.b1);
@@ -924,6 +966,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffFlag);
   volatile int* sLast = sAbort + 1;
   volatile int* sCoop = sAbort + 2;  // last tile: 0 epilogue warp finishes it, 1 consumers, 2 consumers + peers' sums
+  // fused RMSNorm: the consumer warps' per-token sums of z^2 of the tile being handed off, [8 warps][16 tokens]
+  float* sSsq = reinterpret_cast<float*>(smem + C::kOffNorm + (kNormMaxK + 1024) * 2);
   // the CTA's last tile is finished by the consumer warps (plain GEMM instances with bf16 output)
   constexpr bool kCoopLast = !HEAD && !AR && !SILU;
 
@@ -1118,6 +1162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) v[mt][nt][e] = 0.f;
       bool red_ok = false;
+      float peer_ss = 0.f;  // fused RMSNorm: the later CTAs' sums of squares of token `lane` (< 16)
       if (is_red) {
         int ok = 0;
         if (lane == 0 && p.peer_wait_ns > 0) {  // 0: hand off at once
@@ -1138,6 +1183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 2
           for (int cc = c_first + 1; cc <= c_last; ++cc) {  // the tile is each later CTA's first: slot 0
             const float* sl = partials + static_cast<size_t>(2 * cc) * kPartialSlotFloats;
+            if (NORM && lane < 16) peer_ss += __ldcg(sl + kSlotSsq + lane);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -1172,6 +1218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
               for (int e = 0; e < 4; ++e) sPeer[(mt * 32 + lane) * 4 * NT + nt * 4 + e] = v[mt][nt][e];
+          if (NORM && lane < 16) sPeer[MT * 32 * 4 * NT + lane] = peer_ss;
           named_bar_arrive(kBarCoop, kConsumerThreads + 32);
           if (lane == 0) counters[tile] = 0;  // every other contributor has counted itself in: re-arm
         }
@@ -1192,6 +1239,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int e = 0; e < 4; ++e) v[mt][nt][e] += o[nt * 4 + e];
           }
       }
+      float own_ss = 0.f;  // fused RMSNorm: this CTA's sum of squares of token `lane` (< 16) for the tile
+      if constexpr (NORM) {
+        if (lane < 16) {
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) own_ss += sSsq[w * 16 + lane];
+        }
+      }
       if (tcount + 1 < n_ends) named_bar_arrive(kBarFree, kConsumerThreads + 32);
       ++tcount;
 
@@ -1210,6 +1264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __stcg(reinterpret_cast<float2*>(slot + (row + 8) * 8 * NT + col),
                    make_float2(v[mt][nt][2], v[mt][nt][3]));
           }
+        if (NORM && lane < 16) __stcg(slot + kSlotSsq + lane, own_ss);
         __syncwarp();  // the slot stores of all lanes precede lane 0's release
         int last = 0;
         if (lane == 0)  // last only after a reducer gave up waiting
@@ -1217,11 +1272,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                  static_cast<uint32_t>(c_last - c_first);
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          split_reduce_all<BN, NT, HEAD, AR, SILU>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut, ar_epoch,
-                                                   ar_bound);
+          split_reduce_all<BN, NT, HEAD, AR, SILU, NORM>(p, tile, lane, c_first, c_last, counters, partials, sStat, sOut,
+                                                         ar_epoch, ar_bound);
           if constexpr (HEAD) fold_tile<HEAD>(p, lane, sStat, run, run_z);
         }
         continue;
+      }
+      if constexpr (NORM) {  // the whole tile's sums (this CTA's, plus the later CTAs' for a reduced split tile)
+        const float rfac = norm_factor(p, own_ss + peer_ss);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int bq = 0; bq < 2; ++bq) {
+            const float r = __shfl_sync(0xffffffffu, rfac, 8 * nt + 2 * t + bq);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              v[mt][nt][bq] *= r;
+              v[mt][nt][2 + bq] *= r;
+            }
+          }
       }
       finish_tile<BN, NT, HEAD, AR, SILU>(p, tile, lane, v, sc, sOut, sStat, ar_epoch, ar_bound);
       if constexpr (HEAD) fold_tile<HEAD>(p, lane, sStat, run, run_z);
@@ -1258,57 +1327,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(kBarConsumers, kConsumerThreads);
   }
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
-  float* sRms = reinterpret_cast<float*>(smem + C::kOffNorm + (kNormMaxK + 1024) * 2);  // [16] token row scales
   if constexpr (NORM) {
-    // Fused RMSNorm prologue: gamma into shared memory (zero past K), every token's rsqrt(mean(z^2) + eps) with
-    // z = x (+ residual) in fp32, and bf16(z) written to res_out, chunks of 8 columns shared out over the CTAs.
+    // gamma into shared memory, zero past K (the stages' k range reaches past K where the copies zero-fill)
     uint4* sGam = reinterpret_cast<uint4*>(smem + C::kOffNorm);
-    float* sPart = sRms + 16;  // [8 warps][16 tokens]
-    const int kch = p.K / 8;   // K % 8 == 0 (host check)
+    const int kch = p.K / 8;  // K % 8 == 0 (host check)
     for (int i = ctid_early(); i < (kNormMaxK + 1024) / 8; i += kConsumerThreads)
       sGam[i] = i < kch ? __ldg(reinterpret_cast<const uint4*>(p.gamma) + i) : make_uint4(0u, 0u, 0u, 0u);
-    float part[16];
-#pragma unroll
-    for (int m = 0; m < 16; ++m) part[m] = 0.f;
-    for (int i = ctid_early(); i < kch; i += kConsumerThreads) {
-      const bool mine = p.res_out && (i % p.G) == static_cast<int>(blockIdx.x);
-#pragma unroll
-      for (int m = 0; m < 16; ++m) {
-        if (m < p.M) {
-          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx) + i);
-          const uint4 rv = p.res ? __ldg(reinterpret_cast<const uint4*>(p.res + static_cast<int64_t>(m) * p.ldr) + i)
-                                 : make_uint4(0u, 0u, 0u, 0u);
-          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-          const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-          uint32_t zw[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float z0 = __uint_as_float(xw[q] << 16) + __uint_as_float(rw[q] << 16);
-            const float z1 = __uint_as_float(xw[q] & 0xFFFF0000u) + __uint_as_float(rw[q] & 0xFFFF0000u);
-            part[m] = fmaf(z0, z0, part[m]);
-            part[m] = fmaf(z1, z1, part[m]);
-            const __nv_bfloat162 zb = __floats2bfloat162_rn(z0, z1);
-            zw[q] = *reinterpret_cast<const uint32_t*>(&zb);
-          }
-          if (mine)
-            reinterpret_cast<uint4*>(p.res_out + static_cast<int64_t>(m) * p.ldro)[i] = make_uint4(zw[0], zw[1], zw[2], zw[3]);
-        }
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      float v = part[m];
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      if (lane == 0) sPart[warp * 16 + m] = v;
-    }
-    named_bar_sync(kBarConsumers, kConsumerThreads);
-    if (ctid_early() < 16) {
-      float sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) sum += sPart[w * 16 + ctid_early()];
-      sRms[ctid_early()] = ctid_early() < p.M ? rsqrtf(sum / static_cast<float>(p.K) + p.eps) : 0.f;
-    }
     named_bar_sync(kBarConsumers, kConsumerThreads);
   }
   // Warp (u, h), u = warp / 2: m-tile group mg = u % NMW (m-tiles MW * mg ..), weight boxes
@@ -1336,6 +1360,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!p.y_f32 && n_iter > 0)
       last_rs = load_row_scale<BN>(p, p.q > 0 ? p.r + cta + (p.q - 1) * p.G : (it.sk_end - 1) / p.kiters, warp, g);
   }
+
+  // fused RMSNorm: this lane's sum of z^2 over the current tile's stages, for tokens g + 8 nt; counted by the warps
+  // of m-tile group 0 only, which between them read every activation of a stage once
+  float ssq[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) ssq[nt] = 0.f;
 
   float acc[MW][NT][4];
 #pragma unroll
@@ -1373,8 +1403,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             ra = lds128(xbase + C::kXBoxesBytes + nt * 1024 + x_u0);
             rb = lds128(xbase + C::kXBoxesBytes + nt * 1024 + x_u1);
           }
-          xa[nt] = norm_words(xa[nt], ra, ga);
-          xb[nt] = norm_words(xb[nt], rb, gb);
+          float ss = 0.f;
+          uint4 za, zb;
+          xa[nt] = norm_words(xa[nt], ra, ga, ss, za);
+          xb[nt] = norm_words(xb[nt], rb, gb, ss, zb);
+          if (mg == 0) {
+            ssq[nt] += ss;
+            // the new residual bf16(z): written by whichever CTAs stream tile 0 (its stages cover every k once)
+            const int m = g + 8 * nt;
+            if (it.tile == 0 && p.res_out && m < p.M && k0 < p.K) {
+              uint4* dst = reinterpret_cast<uint4*>(p.res_out + static_cast<int64_t>(m) * p.ldro + k0);
+              dst[0] = za;
+              if (k0 + 8 < p.K) dst[1] = zb;
+            }
+          }
         }
       }
       const uint32_t wbase = sW_u32 + s * C::kWBytes + w_off + db * C::kWBoxBytes;
@@ -1419,29 +1461,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tcount > 0) named_bar_sync(kBarFree, kConsumerThreads + 32);  // the previous tile's sums have been read
     {
       float* mine = sRed + (warp * MW * 32 + lane) * 4 * NT;
-      float rs[NT][2];  // fused RMSNorm: tokens 8 nt + 2 t and 8 nt + 2 t + 1 of this lane's accumulators
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        rs[nt][0] = NORM ? sRms[8 * nt + 2 * t] : 1.f;
-        rs[nt][1] = NORM ? sRms[8 * nt + 2 * t + 1] : 1.f;
-      }
 #pragma unroll
       for (int j = 0; j < MW; ++j)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            mine[j * 32 * 4 * NT + nt * 4 + e] = NORM ? acc[j][nt][e] * rs[nt][e & 1] : acc[j][nt][e];
+            mine[j * 32 * 4 * NT + nt * 4 + e] = acc[j][nt][e];
             acc[j][nt][e] = 0.f;
           }
+      if constexpr (NORM) {  // the tile's sums of squares per token (lanes 4 g .. 4 g + 3 hold token g's parts)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float v = ssq[nt];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          if (t == 0) sSsq[warp * 16 + 8 * nt + g] = v;
+          ssq[nt] = 0.f;
+        }
+        if (NT == 1 && lane < 8) sSsq[warp * 16 + 8 + lane] = 0.f;
+      }
     }
     if (kCoopLast && !p.y_f32 && i == n_iter - 1) {  // the CTA's last tile: finished here unless the epilogue
       named_bar_sync(kBarReady, kConsumerThreads + 32);  // warp keeps it (stream-K contribution)
       const int mode = *sCoop;
       if (mode == 2) named_bar_sync(kBarCoop, kConsumerThreads + 32);
       if (mode != 0)
-        coop_finish_tile<BN, NT, MW, NMW>(p, cur_tile, warp, sRed, reinterpret_cast<const float*>(sW), mode == 2,
-                                          sOut, last_rs);
+        coop_finish_tile<BN, NT, MW, NMW, NORM>(p, cur_tile, warp, sRed, reinterpret_cast<const float*>(sW), mode == 2,
+                                                sOut, last_rs, sSsq);
     } else {
       named_bar_arrive(kBarReady, kConsumerThreads + 32);
     }
