@@ -50,6 +50,21 @@ def main() -> int:
         from tests.test_gpu_head import check_draw
         lg = from_dev_bf16(out[0])
         check_draw(lg, V - 3, 0.7, 5, 9, 100, [o.cpu() if o is not None else None for o in out])
+    from qwen_a100_fastpath_b200.w8a16 import w8a16_mm_rmsnorm
+    from tests.test_gpu_rmsnorm import close as norm_close
+    for (N, K, M, silu) in [(2048, 8192, 7, False), (4100, 2048, 12, False), (2000, 1024, 5, True)]:
+        rs = np.random.RandomState(N + M)  # fused RMSNorm on the same schedules (sums of squares handed off too)
+        xb = orc.f32_to_bf16(rs.standard_normal((M, K)).astype(np.float32) * 3.0)
+        rb = orc.f32_to_bf16(rs.standard_normal((M, K)).astype(np.float32))
+        gb = orc.f32_to_bf16((rs.random_sample(K) + 0.5).astype(np.float32))
+        W = rs.randint(-127, 128, size=(N, K)).astype(np.int8)
+        sc = (rs.random_sample(N) * 0.009 + 0.001).astype(np.float32)
+        y, res_out = w8a16_mm_rmsnorm(to_dev_bf16(xb, dev), to_dev_bf16(gb, dev), 1e-6, torch.from_numpy(W).to(dev).t(),
+                                      torch.from_numpy(sc).to(dev), residual=to_dev_bf16(rb, dev), silu_mul=silu)
+        torch.cuda.synchronize()
+        y_ref, r_ref = orc.rmsnorm_w8a16_mm(xb, rb, gb, 1e-6, W, sc, silu=silu)
+        assert np.array_equal(from_dev_bf16(res_out), r_ref)
+        norm_close(from_dev_bf16(y), y_ref, frob=1e-2 if silu else 5e-3)
     from qwen_a100_fastpath_b200.w8a16 import workspace_status
     assert workspace_status() == 0
     print("ok")
