@@ -75,6 +75,11 @@ def parse_args():
                     "gate_up (qf_w8a16_gemm_rmsnorm) against vLLM's RMSNorm in torch followed by the GEMM, at M = 1..16")
     ap.add_argument("--host-overhead", action="store_true", help="eager host time per call of the public entry "
                     "points (enqueue only) against the kernel's device time, o_proj at --m")
+    ap.add_argument("--attn-sweep", action="store_true", help="verification attention (qf_spec_attn) on the reference's "
+                    "attention shapes at context 0..100K beside FlashAttention-2 (and, with --ref-triton, the "
+                    "reference's own Triton kernels)")
+    ap.add_argument("--profile-attn", type=int, default=-1, help="a few launches of the verification attention at this "
+                    "context (Q = 3, one request; the small case for an ncu capture), then exit")
     ap.add_argument("--profile-gemm", default="", help="comma list of qkv,o_proj,gate_up,down,lm_head,lm_head_sample "
                     "(or pf_qkv, pf_o_proj, pf_gate_up, pf_down: the prefill path): a few launches of each at --m (the "
                     "small case for an ncu capture), then exit")
@@ -765,6 +770,111 @@ def run_fused_sweep(args, local: int):
         torch.cuda.empty_cache()
 
 
+def load_reference_spec_attn():
+    """The reference plugin's split-KV attention (plugin/qwen_fastpath/spec_attn.py) from baseline/_ref, or None."""
+    ref_dir = REPO / "baseline" / "_ref"
+    if not (ref_dir / "qwen_fastpath" / "spec_attn.py").exists():
+        return None
+    sys.path.insert(0, str(ref_dir))
+    from qwen_fastpath.spec_attn import gqa_packed_spec_attention as ref
+    return ref
+
+
+def run_attn_sweep(args, local: int):
+    """Verification attention through spec_attn.gqa_packed_spec_attention (qf_spec_attn) on the reference's attention
+    shapes (H = 24, HKV = 4, D = 256, 800-slot pages: bench/test_spec_attn.py of the reference) at context 0..100K
+    and (Q, requests) = (3, 1), (4, 1), (3, 2), (5, 1), beside FlashAttention-2 (vLLM's flash_attn_varlen_func, the
+    path the reference replaces) and, with --ref-triton, the reference's own Triton kernels.  Each time is a CUDA
+    graph of one launch per layer over `n` distinct KV caches (enough layers that together they exceed L2 where memory
+    allows), us per layer; kv_GBps = the KV bytes a layer must read once (sum over requests of seq_len x HKV x 2 x D x
+    2 bytes) / that time, frac = kv_GBps / the measured HBM copy bandwidth."""
+    import torch
+    from qwen_a100_fastpath_b200.spec_attn import gqa_packed_spec_attention, workspace_status
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peak, peak_src = peak_hbm()
+    H, HKV, D, page = 24, 4, 256, 800
+    scale = D ** -0.5
+    stream = torch.cuda.Stream(dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    fa2 = None
+    try:
+        from vllm.vllm_flash_attn import flash_attn_varlen_func as fa2
+    except Exception as e:  # noqa: BLE001 -- FlashAttention-2 from vLLM is a comparator only
+        print(json.dumps({"fa2": f"unavailable: {type(e).__name__}: {str(e)[:120]}"}), flush=True)
+    ref = load_reference_spec_attn() if args.ref_triton else None
+    if ref is not None:
+        import triton
+        print(json.dumps({"reference_triton": triton.__version__, "module": ref.__module__}), flush=True)
+    if args.profile_attn >= 0:
+        cases = [(args.profile_attn, 3, 1)]
+    else:
+        cases = [(c, q, b) for c in (0, 50, 1000, 8000, 38000, 100000) for q, b in ((3, 1), (4, 1), (3, 2), (5, 1))]
+    print(json.dumps({"peak_hbm_GBps": peak, "peak_source": peak_src}), flush=True)
+    for ctx, Q, B in cases:
+        L = ctx + Q
+        lens = [max(L - 7 * i, 1) for i in range(B)]
+        pages = (L + page - 1) // page
+        nblk = B * pages + 1
+        layer_bytes = nblk * HKV * page * 2 * D * 2
+        n = int(min(16, max(1, (4 * 126e6) // layer_bytes)))
+        caches = []
+        for _ in range(n):
+            kv = torch.randn(nblk, HKV, page, 2 * D, device=dev, generator=g).to(torch.bfloat16)
+            bt = torch.randperm(nblk, device=dev, generator=g)[: B * pages].to(torch.int32).view(B, pages)
+            caches.append((kv, *kv.transpose(1, 2).split(D, dim=-1), bt))
+        q = torch.randn(B * Q, H, D, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        seq_lens = torch.tensor(lens, dtype=torch.int32, device=dev)
+        cu_q = torch.arange(0, B + 1, device=dev, dtype=torch.int32) * Q
+        kv_bytes = sum(lens) * HKV * 2 * D * 2
+        if args.profile_attn >= 0:
+            for i in range(3):
+                gqa_packed_spec_attention(q, caches[i % n][1], caches[i % n][2], out, seq_lens, caches[i % n][3], B, Q,
+                                          HKV, scale)
+            torch.cuda.synchronize()
+            print(json.dumps({"profile_attn": ctx, "launches": 3, "status": workspace_status(dev)}), flush=True)
+            return
+
+        def ours(i):
+            gqa_packed_spec_attention(q, caches[i][1], caches[i][2], out, seq_lens, caches[i][3], B, Q, HKV, scale)
+
+        def fa(i):
+            fa2(q=q, k=caches[i][1], v=caches[i][2], out=out, cu_seqlens_q=cu_q, max_seqlen_q=Q, seqused_k=seq_lens,
+                max_seqlen_k=131072, softmax_scale=scale, causal=True, block_table=caches[i][3], fa_version=2)
+
+        def reference(i):
+            ref(q, caches[i][1], caches[i][2], out, seq_lens, caches[i][3], B, Q, HKV, scale)
+
+        row = {"ctx": ctx, "Q": Q, "reqs": B, "layers_in_graph": n, "kv_bytes": kv_bytes}
+        for tag, fn in (("ours", ours), ("fa2", fa if fa2 else None), ("ref_triton", reference if ref else None)):
+            if fn is None:
+                continue
+            try:
+                with torch.cuda.stream(stream):
+                    for i in range(n):
+                        fn(i)
+                torch.cuda.synchronize()
+                reps = max(1, 32 // n)
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for _ in range(reps):
+                        for i in range(n):
+                            fn(i)
+                us = time_graph(gr, stream, 5, 2) / (reps * n) * 1e3
+                del gr
+                row[tag + "_us"] = round(us, 2)
+                row[tag + "_kv_GBps"] = round(kv_bytes / us / 1e3, 1)
+            except Exception as e:  # noqa: BLE001 -- a comparator that cannot run on this box is reported, not fatal
+                row[tag] = f"unavailable: {type(e).__name__}: {str(e)[:120]}"
+        if "ours_us" in row:
+            row["ours_frac_of_measured"] = round(row["ours_kv_GBps"] / peak, 3)
+        row["status"] = workspace_status(dev)
+        print(json.dumps(row), flush=True)
+        del caches
+        torch.cuda.empty_cache()
+
+
 def run_host_overhead(args, local: int):
     """Host cost of one eager call (argument checks, ctypes, tensor-map encoding, launch) of the C-ABI entry point,
     of ``w8a16_mm`` and of the ``qf_int8_linear`` op body, against the device time of the same launch, for o_proj at
@@ -845,6 +955,10 @@ def main():
     if args.fused_sweep:
         if rank == 0:
             run_fused_sweep(args, local)
+        return
+    if args.attn_sweep or args.profile_attn >= 0:
+        if rank == 0:
+            run_attn_sweep(args, local)
         return
     run_ours(args, rank, world, local)
 

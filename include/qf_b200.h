@@ -152,6 +152,28 @@ size_t qf_w8a8_workspace_bytes(int M, int K);
 int qf_w8a8_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* w_scale, const void* bias,
                  void* y, int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, unsigned flags, void* stream);
 
+/* ---- speculative-verification attention (QWEN_FAST_ATTN) -------------------------------------------------------
+ * Replaces gqa_packed_spec_attention (plugin/qwen_fastpath/spec_attn.py:139-173), the path patch_flash_attention
+ * routes uniform speculative-decode batches to (patches.py:10-69).  num_reqs requests x q_len query tokens each
+ * (token b * q_len + qi); query qi of request b attends the cached keys [0, seq_lens[b] - q_len + qi] (this step's
+ * keys are already in the cache); a row with no key gives zeros.  q: bf16 [num_reqs * q_len][num_heads][head_size]
+ * with element strides (sq_t, sq_h, 1); k_cache / v_cache: bf16 [num_blocks][page_size][num_kv_heads][head_size]
+ * views with element strides (s_b, s_t, s_h, 1) (any order of slot and head strides, the same for both);
+ * block_table: int32 [num_reqs][*] (row stride s_bt; the page of slot pos is block_table[b][pos / page_size]);
+ * seq_lens: int32 [num_reqs]; out: bf16, same layout as q with strides (so_t, so_h, 1).  Softmax scale `scale`;
+ * num_heads a multiple of num_kv_heads; head_size 64, 128 or 256; q_len * num_heads / num_kv_heads <= 64;
+ * page_size a multiple of 16; q, caches and out 16-byte aligned with strides multiples of 8 elements.  The workspace
+ * (>= qf_spec_attn_workspace_bytes(...) for the current device, 256-byte aligned; word 0 is a sticky error flag read
+ * by qf_workspace_status) holds the split partials; it need not be zeroed.  One or two launches on `stream`, no host
+ * synchronisation and no host read of device data (CUDA-graph capturable); QF_FLAG_PDL lets the first launch overlap
+ * the previous kernel's tail. */
+size_t qf_spec_attn_workspace_bytes(int num_reqs, int q_len, int num_heads, int num_kv_heads, int head_size);
+int qf_spec_attn(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache, int64_t sk_b, int64_t sk_t,
+                 int64_t sk_h, const void* v_cache, int64_t sv_b, int64_t sv_t, int64_t sv_h, int num_blocks,
+                 int page_size, const int32_t* block_table, int64_t s_bt, const int32_t* seq_lens, void* out,
+                 int64_t so_t, int64_t so_h, int num_reqs, int q_len, int num_heads, int num_kv_heads, int head_size,
+                 float scale, void* ws, size_t ws_bytes, unsigned flags, void* stream);
+
 /* The W8A16 GEMM with the RMSNorm that precedes qkv and gate_up in a decoder layer fused into it (the reference plugin
  * leaves the norm to vLLM's RMSNorm: z = x + residual, new residual = bf16(z), normalized activation
  * bf16(bf16(z * rsqrt(mean(z^2) + eps)) * gamma)).  Here the activation fed to the contraction is bf16(bf16(z) * gamma)

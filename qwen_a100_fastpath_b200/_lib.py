@@ -54,6 +54,12 @@ SIGNATURES = [
     ("qf_w8a8_gemm", _c.c_int,
      [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int,
       _c.c_int, _c.c_int, _c.c_void_p, _c.c_size_t, _c.c_uint, _c.c_void_p]),
+    ("qf_spec_attn_workspace_bytes", _c.c_size_t, [_c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
+    ("qf_spec_attn", _c.c_int,
+     [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_int64,
+      _c.c_int64, _c.c_int64, _c.c_int, _c.c_int, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64,
+      _c.c_int64, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_float, _c.c_void_p, _c.c_size_t, _c.c_uint,
+      _c.c_void_p]),
     ("qf_quantize_rows_int8", _c.c_int,
      [_c.c_void_p, _c.c_int64, _c.c_int, _c.c_int, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p]),
     ("qf_allreduce_buffer_bytes", _c.c_size_t, [_c.c_int]),

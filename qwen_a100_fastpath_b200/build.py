@@ -20,7 +20,7 @@ INCLUDE = PKG.parent / "include"
 LIB = PKG / "libqf_b200.so"
 TORCH_OPS = PKG / "_qf_torch_ops.so"
 TORCH_OPS_SOURCE = "qf_torch_ops.cpp"
-SOURCES = ["qf_w8a16.cu", "qf_allreduce.cu", "qf_quant.cu", "qf_w8a8.cu"]
+SOURCES = ["qf_w8a16.cu", "qf_allreduce.cu", "qf_quant.cu", "qf_w8a8.cu", "qf_spec_attn.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

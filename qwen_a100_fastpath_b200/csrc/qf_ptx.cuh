@@ -1,8 +1,9 @@
 // qf_ptx.cuh -- thin inline-PTX wrappers used by the sm_100a kernels of libqf_b200.
 //
 // Only documented PTX ISA forms are used: mbarrier (arrive / expect_tx / try_wait.parity), the tiled TMA
-// load cp.async.bulk.tensor.2d (no multicast), createpolicy for L2 eviction hints, griddepcontrol for
-// programmatic dependent launch, bar.sync on named barriers and mma.sync m16n8k16 bf16.
+// loads cp.async.bulk.tensor.2d / .4d (no multicast), createpolicy for L2 eviction hints, griddepcontrol for
+// programmatic dependent launch, bar.sync on named barriers, ldmatrix (.trans), ex2.approx, mma.sync m16n8k16
+// bf16 / f16, and the tcgen05 forms listed further down.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -72,6 +73,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Four-dimensional tiled load (same form, coordinates c0 innermost .. c3 outermost).
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Brings a kernel-parameter tensor map into the TMA unit's descriptor cache before its first copy.
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -135,6 +146,28 @@ __device__ __forceinline__ void mma_f16_m16n8k16(float (&d)[4], uint32_t a0, uin
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Four 8x8 b16 matrices from shared memory; lane l supplies the address of row (l % 8) of matrix (l / 8), and
+// register j receives matrix j in the mma fragment layout (thread (g, t) holds row g, columns 2t, 2t + 1; with .trans
+// the matrix is transposed on the way).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// 2^x by the special-function unit (PTX ex2.approx.ftz.f32: relative error about 2^-22; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void lds64(uint32_t addr, uint32_t& a, uint32_t& b) {

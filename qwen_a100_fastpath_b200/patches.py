@@ -1,7 +1,11 @@
 """vLLM patches of the B200 W8A16 decode path (the drop-in boundary).
 
 Same patch targets, guards and fallbacks as ``qwen_fastpath.patches`` of EurekaZang/qwen-a100-fastpath
-(plugin/qwen_fastpath/patches.py:72-189); the kernels behind them are ``libqf_b200.so``:
+(plugin/qwen_fastpath/patches.py:10-189); the kernels behind them are ``libqf_b200.so``:
+
+* ``patch_flash_attention``: ``FlashAttentionImpl.forward`` sends uniform speculative-verification batches
+  (every request with the same ``1 < Q <= 8`` query tokens) to the split-KV GQA-packed kernel ``qf_spec_attn``
+  (patches.py:10-69, spec_attn.py:139-173); everything else stays on FlashAttention.
 
 * ``patch_int8_linear``: ``CutlassInt8ScaledMMLinearKernel.apply_weights(self, layer, x, bias=None)`` routes
   dynamic symmetric per-token W8A8 linears (patches.py:110) to the opaque custom op
@@ -25,6 +29,105 @@ import logging
 import torch
 
 logger = logging.getLogger("vllm.qwen_fastpath")
+
+MAX_SPEC_QUERY_LEN = 8
+
+
+# ----------------------------------------------------------------------------------------------
+# QWEN_FAST_ATTN
+# ----------------------------------------------------------------------------------------------
+def spec_attn_eligible(impl) -> bool:
+    """Whether a FlashAttention layer can take the split-KV verification kernel (the reference's layer guard,
+    patches.py:23-42, with attributes read defensively across vLLM versions; the FlashAttention version does not
+    matter here because the kernel only reads the paged cache).  Cached on the layer."""
+    ok = getattr(impl, "_qf_eligible", None)
+    if ok is None:
+        from vllm.v1.attention.backends import flash_attn as fa
+        from .spec_attn import supported
+        sw = getattr(impl, "sliding_window", None)
+        ok = bool(
+            getattr(impl, "attn_type", None) == fa.AttentionType.DECODER
+            and getattr(impl, "dcp_world_size", 1) == 1
+            and not getattr(impl, "fa4_hd256", False)
+            and (sw is None or tuple(sw) == (-1, -1))
+            and getattr(impl, "alibi_slopes", None) is None
+            and not getattr(impl, "logits_soft_cap", None)
+            and getattr(impl, "sinks", None) is None
+            and not fa.is_quantized_kv_cache(impl.kv_cache_dtype)
+            and impl.num_heads % impl.num_kv_heads == 0
+            and impl.head_size in (64, 128, 256)
+            and supported(impl.num_heads, impl.num_kv_heads, impl.head_size, 2, 16)
+            and getattr(impl, "kv_sharing_target_layer_name", None) is None)
+        impl._qf_eligible = ok
+    return ok
+
+
+def spec_attn_caches(kv_cache: torch.Tensor, head_size: int):
+    """(key_cache, value_cache) views ``[num_blocks, page, num_kv_heads, head_size]`` of a layer's KV cache: vLLM's
+    FlashAttention layout ``[2, num_blocks, page, HKV, D]`` (``unbind(0)``), or the interleaved layout the reference
+    reads (``[num_blocks, HKV, page, 2 D]``, ``transpose(1, 2).split(D, -1)``, patches.py:55); None otherwise."""
+    if kv_cache.dim() == 5 and kv_cache.shape[0] == 2 and kv_cache.shape[-1] == head_size:
+        return kv_cache.unbind(0)
+    if kv_cache.dim() == 4 and kv_cache.shape[-1] == 2 * head_size:
+        k, v = kv_cache.transpose(1, 2).split(head_size, dim=-1)
+        return k, v
+    return None
+
+
+def spec_attn_forward(impl, query, kv_cache, md, output, output_scale=None, output_block_scale=None):
+    """The body of the patched ``FlashAttentionImpl.forward`` for one call: runs the split-KV kernel and returns
+    ``output`` for a uniform speculative-verification batch (every request has the same ``1 < Q <= 8`` query tokens,
+    causal, no cascade), None when the call must stay on FlashAttention (patches.py:44-66 of the reference)."""
+    if (md is None or output_scale is not None or output_block_scale is not None
+            or not 1 < md.max_query_len <= MAX_SPEC_QUERY_LEN or getattr(md, "use_cascade", False)
+            or getattr(md, "causal", True) is not True
+            or getattr(md, "mm_prefix_query_range_tensor", None) is not None
+            or getattr(md, "rswa_prefix_lens", None) is not None
+            or query.dtype != torch.bfloat16 or not spec_attn_eligible(impl)):
+        return None
+    num_reqs = md.query_start_loc.shape[0] - 1
+    q_len = md.max_query_len
+    if md.num_actual_tokens != num_reqs * q_len:  # uniform: every request has exactly q_len tokens
+        return None
+    caches = spec_attn_caches(kv_cache, impl.head_size)
+    if caches is None or caches[0].dtype != torch.bfloat16:
+        return None
+    from .spec_attn import gqa_packed_spec_attention, supported
+    key_cache, value_cache = caches
+    if not supported(impl.num_heads, impl.num_kv_heads, impl.head_size, q_len, key_cache.shape[1]):
+        return None
+    q3 = query.view(query.shape[0], impl.num_heads, impl.head_size)
+    o3 = output.view(output.shape[0], impl.num_heads, impl.head_size)
+    gqa_packed_spec_attention(q3, key_cache, value_cache, o3, md.seq_lens, md.block_table, num_reqs, q_len,
+                              impl.num_kv_heads, impl.scale)
+    return output
+
+
+def patch_flash_attention() -> bool:
+    """Route uniform speculative-decode batches (every request has Q = 1 + k query tokens, 1 < Q <= 8) through the
+    split-KV GQA-packed kernel; prefill, mixed batches and Q == 1 stay on FlashAttention (patches.py:10-69)."""
+    try:
+        from vllm.v1.attention.backends import flash_attn as fa
+    except Exception as e:  # noqa: BLE001 -- any import failure of the backend disables only this patch
+        logger.info("qwen_fastpath: attention patch skipped (%s)", e)
+        return False
+    orig_forward = fa.FlashAttentionImpl.forward
+    if getattr(orig_forward, "_qwen_fastpath", False):
+        return False
+
+    def forward(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale=None,
+                output_block_scale=None):
+        out = spec_attn_forward(self, query, kv_cache, attn_metadata, output, output_scale, output_block_scale)
+        if out is not None:
+            return out
+        return orig_forward(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale,
+                            output_block_scale)
+
+    forward._qwen_fastpath = True
+    forward._qf_orig = orig_forward
+    fa.FlashAttentionImpl.forward = forward
+    logger.info("qwen_fastpath: split-KV GQA-packed attention enabled for speculative-decode verification")
+    return True
 
 
 # ----------------------------------------------------------------------------------------------

@@ -86,8 +86,11 @@ def test_register_patches_installed_vllm(monkeypatch):
     cls = vllm_cutlass.CutlassInt8ScaledMMLinearKernel
     orig = cls.apply_weights
     from vllm.model_executor.layers.linear import RowParallelLinear
+    from vllm.v1.attention.backends import flash_attn as fa
     orig_row = RowParallelLinear.forward
+    orig_attn = fa.FlashAttentionImpl.forward
     try:
+        monkeypatch.setenv("QWEN_FAST_ATTN", "1")
         monkeypatch.setenv("QWEN_FAST_LINEAR", "1")
         monkeypatch.setenv("QWEN_FAST_DRAFT_HEAD", "1")
         monkeypatch.setattr(plugin, "_registered", False)
@@ -106,9 +109,12 @@ def test_register_patches_installed_vllm(monkeypatch):
         assert getattr(qwen3_5_mtp.Qwen3_5MTP.compute_logits, "_qwen_fastpath", False)
         assert getattr(RowParallelLinear.forward, "_qwen_fastpath", False)
         assert patches.patch_row_parallel() is False                     # idempotent
+        assert getattr(fa.FlashAttentionImpl.forward, "_qwen_fastpath", False)
+        assert patches.patch_flash_attention() is False                  # idempotent
     finally:
         cls.apply_weights = getattr(cls.apply_weights, "_qf_orig", orig)
         RowParallelLinear.forward = orig_row
+        fa.FlashAttentionImpl.forward = orig_attn
 
 
 def test_switches_off(monkeypatch):
@@ -118,13 +124,85 @@ def test_switches_off(monkeypatch):
     monkeypatch.setattr(patches, "patch_int8_linear", lambda: called.append("linear"))
     monkeypatch.setattr(patches, "patch_row_parallel", lambda: called.append("row"))
     monkeypatch.setattr(patches, "patch_draft_lm_head", lambda: called.append("head"))
+    monkeypatch.setattr(patches, "patch_flash_attention", lambda: called.append("attn"))
     monkeypatch.setattr(plugin, "_registered", False)
+    monkeypatch.setenv("QWEN_FAST_ATTN", "0")
     monkeypatch.setenv("QWEN_FAST_LINEAR", "0")
     monkeypatch.setenv("QWEN_FAST_DRAFT_HEAD", "1")
     plugin.register()
     assert called == ["head"]
     monkeypatch.setattr(plugin, "_registered", False)
+    monkeypatch.setenv("QWEN_FAST_ATTN", "1")
     monkeypatch.setenv("QWEN_FAST_LINEAR", "1")
     monkeypatch.setenv("QWEN_FAST_DRAFT_HEAD", "0")
     plugin.register()
-    assert called == ["head", "linear", "row"]
+    assert called == ["head", "attn", "linear", "row"]
+
+
+# ---------------------------------------------------------------------------------------------- QWEN_FAST_ATTN
+def fake_attn_impl(**kw):
+    import types
+    from vllm.v1.attention.backends import flash_attn as fa
+    d = dict(attn_type=fa.AttentionType.DECODER, dcp_world_size=1, sliding_window=(-1, -1), alibi_slopes=None,
+             logits_soft_cap=None, sinks=None, kv_cache_dtype="auto", num_heads=24, num_kv_heads=4, head_size=256,
+             kv_sharing_target_layer_name=None, scale=256 ** -0.5)
+    d.update(kw)
+    return types.SimpleNamespace(**d)
+
+
+def fake_md(num_reqs, q_len, num_tokens=None, **kw):
+    import types
+    d = dict(max_query_len=q_len, use_cascade=False, causal=True,
+             query_start_loc=torch.arange(num_reqs + 1, dtype=torch.int32) * q_len,
+             num_actual_tokens=num_reqs * q_len if num_tokens is None else num_tokens,
+             seq_lens=torch.full((num_reqs,), 100, dtype=torch.int32),
+             block_table=torch.zeros((num_reqs, 4), dtype=torch.int32))
+    d.update(kw)
+    return types.SimpleNamespace(**d)
+
+
+@pytest.mark.slow
+def test_spec_attn_routing(monkeypatch):
+    """patches.spec_attn_forward (the body of the patched FlashAttentionImpl.forward, patches.py:44-66 of the
+    reference): uniform batches with 1 < Q <= 8 go to the kernel with the right cache views for both layouts;
+    everything else returns None (FlashAttention)."""
+    pytest.importorskip("vllm.v1.attention.backends.flash_attn")
+    from qwen_a100_fastpath_b200 import patches, spec_attn
+    calls = []
+
+    def record(q3, kc, vc, o3, seq_lens, bt, num_reqs, Q, hkv, scale):
+        calls.append((tuple(q3.shape), tuple(kc.shape), kc.stride(), tuple(vc.shape), num_reqs, Q, hkv, scale))
+        return o3
+
+    monkeypatch.setattr(spec_attn, "gqa_packed_spec_attention", record)
+    H, HKV, D, page, nb = 24, 4, 256, 800, 6
+    vllm_cache = torch.zeros((2, nb, page, HKV, D), dtype=torch.bfloat16)   # vLLM FlashAttention layout
+    ref_cache = torch.zeros((nb, HKV, page, 2 * D), dtype=torch.bfloat16)   # the reference's interleaved layout
+    q = torch.zeros((8, H, D), dtype=torch.bfloat16)
+    out = torch.zeros((8, H * D), dtype=torch.bfloat16)
+    impl = fake_attn_impl()
+    assert patches.spec_attn_forward(impl, q[:6], vllm_cache, fake_md(2, 3), out[:6]) is not None
+    assert calls[-1][:2] == ((6, H, D), (nb, page, HKV, D)) and calls[-1][4:7] == (2, 3, HKV)
+    assert calls[-1][2] == vllm_cache[0].stride()
+    assert patches.spec_attn_forward(impl, q[:8], ref_cache, fake_md(2, 4), out[:8]) is not None
+    assert calls[-1][1] == (nb, page, HKV, D) and calls[-1][2] == ref_cache.transpose(1, 2).stride()
+    n = len(calls)
+    for md in (fake_md(3, 1), fake_md(1, 9), fake_md(2, 3, num_tokens=5), fake_md(2, 3, use_cascade=True),
+               fake_md(2, 3, causal=False), None):
+        assert patches.spec_attn_forward(impl, q[:6], vllm_cache, md, out[:6]) is None
+    assert patches.spec_attn_forward(impl, q[:6].half(), vllm_cache, fake_md(2, 3), out[:6]) is None
+    assert patches.spec_attn_forward(impl, q[:6], vllm_cache, fake_md(2, 3), out[:6],
+                                     output_scale=torch.ones(1)) is None
+    assert patches.spec_attn_forward(impl, q[:6], vllm_cache.half(), fake_md(2, 3), out[:6]) is None
+    for bad in (dict(sliding_window=(127, 0)), dict(logits_soft_cap=30.0), dict(head_size=96),
+                dict(num_heads=66, num_kv_heads=1), dict(kv_sharing_target_layer_name="x")):
+        assert patches.spec_attn_forward(fake_attn_impl(**bad), q[:6], vllm_cache, fake_md(2, 3), out[:6]) is None
+    g8 = fake_attn_impl(num_heads=32, num_kv_heads=4, head_size=128)             # G = 8, Q = 8: 64 packed rows
+    q8, o8 = torch.zeros((8, 32, 128), dtype=torch.bfloat16), torch.zeros((8, 32 * 128), dtype=torch.bfloat16)
+    assert patches.spec_attn_forward(g8, q8, torch.zeros((2, nb, 32, 4, 128), dtype=torch.bfloat16),
+                                     fake_md(1, 8), o8) is not None
+    g16 = fake_attn_impl(num_heads=64, num_kv_heads=4, head_size=128)            # G = 16, Q = 5: 80 rows, not taken
+    q16, o16 = torch.zeros((5, 64, 128), dtype=torch.bfloat16), torch.zeros((5, 64 * 128), dtype=torch.bfloat16)
+    assert patches.spec_attn_forward(g16, q16, torch.zeros((2, nb, 32, 4, 128), dtype=torch.bfloat16),
+                                     fake_md(1, 5), o16) is None
+    assert len(calls) == n + 1

@@ -163,3 +163,46 @@ def head_sample(**kw):
 ])
 def test_head_sample_argument_validation(kw, code):
     assert head_sample(**kw) == code
+
+
+def spec_attn(**kw):
+    a = dict(q=FAKE, sq_t=24 * 256, sq_h=256, k=FAKE, sk_b=800 * 4 * 512, sk_t=512, sk_h=800 * 512, v=FAKE + 512,
+             sv_b=800 * 4 * 512, sv_t=512, sv_h=800 * 512, num_blocks=8, page=800, bt=FAKE, s_bt=8, lens=FAKE,
+             out=FAKE, so_t=24 * 256, so_h=256, num_reqs=1, q_len=3, num_heads=24, num_kv_heads=4, head_size=256,
+             scale=0.0625, ws=FAKE, ws_bytes=1 << 30, flags=0, stream=None)
+    a.update(kw)
+    return _lib.LIB.qf_spec_attn(*a.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q_len=0), -2),
+    (dict(num_heads=25), -2),                  # not a multiple of num_kv_heads
+    (dict(head_size=96), -2),
+    (dict(q_len=11), -2),                      # Q * G = 66 > 64
+    (dict(page=8), -2),
+    (dict(page=40), -2),                       # not a multiple of 16
+    (dict(num_blocks=0), -2),
+    (dict(scale=0.0), -1),
+    (dict(scale=float("nan")), -1),
+    (dict(lens=None), -1),
+    (dict(ws=None), -1),
+    (dict(q=FAKE + 8), -4),
+    (dict(k=FAKE + 2), -4),
+    (dict(sq_h=260), -3),                      # not a multiple of 8 elements
+    (dict(sk_t=0), -3),
+    (dict(sv_t=800 * 512 * 4, sv_h=512), -3),  # V's slot / head order differs from K's
+    (dict(s_bt=0), -3),
+    (dict(ws=FAKE + 64), -4),
+])
+def test_spec_attn_argument_validation(kw, code):
+    assert spec_attn(**kw) == code
+    assert len(_lib.LIB.qf_last_error_detail()) > 0
+
+
+def test_spec_attn_empty_batch_and_workspace():
+    assert spec_attn(num_reqs=0) == 0
+    lib = _lib.LIB
+    assert lib.qf_spec_attn_workspace_bytes(0, 3, 24, 4, 256) == 256
+    # no GPU here: sized for 160 SMs, i.e. 160 / (num_reqs * HKV) = 40 splits of the 4 heads x 18 packed rows
+    rows = 1 * 4 * 40 * 18
+    assert lib.qf_spec_attn_workspace_bytes(1, 3, 24, 4, 256) == 256 + (rows * 256 * 4 + 255) // 256 * 256 + rows * 4
