@@ -40,6 +40,8 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -293,25 +295,33 @@ __global__ void __launch_bounds__(SaGeo<D, MT>::kThreads, 1)
         }
         __syncwarp();
       }
-      // S = Q K^T for 16 rows x 16 slots, two accumulator sets (even / odd k-steps) for independent MMA chains
+      // S = Q K^T for 16 rows x 16 slots, two accumulator sets (even / odd k-steps) for independent MMA chains; the
+      // fragments of k-step kk + 1 are loaded before the MMAs of kk is issued
       float sa[2][4], sb[2][4];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
+      uint32_t fa[2][4], fb[2][4];
+      ldsm_x4(q_u + sw_off(a_row, a_ch, C::kQBoxBytes), fa[0][0], fa[0][1], fa[0][2], fa[0][3]);
+      ldsm_x4(kb + sw_off(k_tok, k_ch, C::kBoxBytes), fb[0][0], fb[0][1], fb[0][2], fb[0][3]);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-        ldsm_x4(q_u + sw_off(a_row, 2 * kk + a_ch, C::kQBoxBytes), a0, a1, a2, a3);
-        ldsm_x4(kb + sw_off(k_tok, 2 * kk + k_ch, C::kBoxBytes), b0, b1, b2, b3);
-        if (kk & 1) {
-          mma_bf16_m16n8k16(sb[0], a0, a1, a2, a3, b0, b1);
-          mma_bf16_m16n8k16(sb[1], a0, a1, a2, a3, b2, b3);
-        } else {
-          mma_bf16_m16n8k16(sa[0], a0, a1, a2, a3, b0, b1);
-          mma_bf16_m16n8k16(sa[1], a0, a1, a2, a3, b2, b3);
+        const int c = kk & 1;
+        if (kk + 1 < D / 16) {
+          ldsm_x4(q_u + sw_off(a_row, 2 * (kk + 1) + a_ch, C::kQBoxBytes), fa[c ^ 1][0], fa[c ^ 1][1], fa[c ^ 1][2],
+                  fa[c ^ 1][3]);
+          ldsm_x4(kb + sw_off(k_tok, 2 * (kk + 1) + k_ch, C::kBoxBytes), fb[c ^ 1][0], fb[c ^ 1][1], fb[c ^ 1][2],
+                  fb[c ^ 1][3]);
         }
+        float (&s0)[4] = c ? sb[0] : sa[0];
+        float (&s1)[4] = c ? sb[1] : sa[1];
+        mma_bf16_m16n8k16(s0, fa[c][0], fa[c][1], fa[c][2], fa[c][3], fb[c][0], fb[c][1]);
+        mma_bf16_m16n8k16(s1, fa[c][0], fa[c][1], fa[c][2], fa[c][3], fb[c][2], fb[c][3]);
       }
+      // the first V fragments do not depend on P: load them before the softmax
+      uint32_t fv[2][4];
+      ldsm_x4_trans(vb + sw_off(v_tok, v_ch, C::kBoxBytes), fv[0][0], fv[0][1], fv[0][2], fv[0][3]);
       // scaled scores (base 2), masked past the chunk's end and past each row's causal limit
       const bool unmasked = pos0 + kSaSlice <= end && pos0 + kSaSlice - 1 <= lim0;
       float x[2][4];
@@ -364,10 +374,12 @@ __global__ void __launch_bounds__(SaGeo<D, MT>::kThreads, 1)
       const uint32_t pa3 = pack_bf16x2(pr[1][2], pr[1][3]);
 #pragma unroll
       for (int j = 0; j < D / 16; ++j) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_trans(vb + sw_off(v_tok, 2 * j + v_ch, C::kBoxBytes), b0, b1, b2, b3);
-        mma_bf16_m16n8k16(o[2 * j], pa0, pa1, pa2, pa3, b0, b1);
-        mma_bf16_m16n8k16(o[2 * j + 1], pa0, pa1, pa2, pa3, b2, b3);
+        const int c = j & 1;
+        if (j + 1 < D / 16)
+          ldsm_x4_trans(vb + sw_off(v_tok, 2 * (j + 1) + v_ch, C::kBoxBytes), fv[c ^ 1][0], fv[c ^ 1][1], fv[c ^ 1][2],
+                        fv[c ^ 1][3]);
+        mma_bf16_m16n8k16(o[2 * j], pa0, pa1, pa2, pa3, fv[c][0], fv[c][1]);
+        mma_bf16_m16n8k16(o[2 * j + 1], pa0, pa1, pa2, pa3, fv[c][2], fv[c][3]);
       }
     }
     __syncwarp();
@@ -550,6 +562,436 @@ __global__ void __launch_bounds__(256) spec_attn_merge_kernel(const SaParams p) 
   }
 }
 
+// =============================================================================================== tcgen05 path
+// Head sizes 128 and 256: the score and value products run on the 5th-generation tensor cores, one 64-token tile of
+// the chunk at a time, accumulators in tensor memory.
+//   S [64 rows x 64 tokens] = Q [rows x D] . K^T      (M = 64: the R = Q * G packed rows, zero-padded; N = 64 tokens;
+//                                                       K-major A from the query tile, K-major B from the K tile)
+//   O [64 rows x D] += P [rows x 64 tokens] . V        (M = 64, N = D; P^T-free: P is the K-major A operand, V is
+//                                                       read in place as an MN-major B operand)
+// An M = 64 accumulator puts row r in tensor-memory lane r % 16 + 32 (r / 16): lanes 0-15 of each of the four softmax
+// warps own a row each, so a row's maximum, exponentials and sum are thread-local (no shuffles, no exchange between
+// warps).  The padding rows cost tensor-core time only, which the kernel has to spare (the MMAs are a few percent of
+// it).  Roles (6 warps): warp 0 streams K and V with TMA into a ring of 8 KiB pieces (K: one 64-column block of the
+// tile's 64 tokens; V: 16 (D = 256) or 32 (D = 128) tokens of every column) -- lane q arms piece q of the tile, then
+// every lane issues one 16-token box, since one issuing thread caps the copy rate well below HBM bandwidth; warp 1
+// allocates tensor memory and lane 0 issues the MMAs (S of tile i + 1 before P V of tile i, so the softmax of tile i
+// overlaps the next scores) and releases pieces with tcgen05.commit; warps 2-5 are the softmax: base-2 scores of the
+// thread's row from tcgen05.ld, a reference maximum raised only when the row's maximum grows by more than 2^8 (then
+// the row's O and sum are rescaled in place), P rounded to bf16 and stored as the row of the A operand, and at the end
+// O / l written as outputs or split partials like the mma.sync kernel.
+template <int D> struct SaTcGeo {
+  static constexpr int kThreads = 192;
+  static constexpr int kTile = 64;                   // tokens per tile
+  static constexpr int kRows = 64;                   // M of both products
+  static constexpr int kPiece = 8192;
+  static constexpr int kKPieces = D / 64;            // K: [64 tokens][64 columns] per piece
+  static constexpr int kVTok = kPiece / (2 * D);     // V: tokens per piece, all D columns
+  static constexpr int kVPieces = kTile / kVTok;
+  static constexpr int kPiecesPerTile = kKPieces + kVPieces;
+  static constexpr int kVLbo = kVTok * 128;          // V piece: 64-column blocks of kVTok 128-byte rows
+  static constexpr int kQBytes = (D / 64) * kRows * 128;
+  static constexpr int kPBytes = kRows * 128;        // P: [64 rows][64 tokens x 2 B]
+  static constexpr int kMiscBytes = 4 * kSaBtCache + 1024;
+  static constexpr int kRingFit = (227 * 1024 - kQBytes - 2 * kPBytes - kMiscBytes - 1024) / kPiece;
+  static constexpr int kRing = kRingFit > 32 ? 32 : kRingFit;
+  static constexpr int kOffQ = kRing * kPiece;
+  static constexpr int kOffP = kOffQ + kQBytes;
+  static constexpr int kOffBt = kOffP + 2 * kPBytes;
+  static constexpr int kOffBar = kOffBt + 4 * kSaBtCache;
+  // barriers: full[kRing], empty[kRing], s_full[2], s_free[2], p_full[2], pv_done[2], drain
+  static constexpr int kNumBars = 2 * kRing + 9;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;             // tensor-memory address, abort flag
+  static constexpr int kSmemBytes = kOffMisc + 16 + 1024;
+  static constexpr uint32_t kColS = 0;                               // S buffers b at b * 64
+  static constexpr uint32_t kColO = 2 * kTile;                       // O: D columns
+  static constexpr uint32_t kTmemCols = 2 * kTile + D <= 256 ? 256 : 512;
+  static_assert(kRing >= 2 * kPiecesPerTile, "ring shallower than two tiles");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+  static_assert(D == 128 || D == 256, "tcgen05 path head sizes");
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    spec_attn_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                        const SaParams p) {
+  using C = SaTcGeo<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::kRing;
+  uint64_t* s_full = bars + 2 * C::kRing;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_full + 4;
+  uint64_t* pv_done = s_full + 6;
+  uint64_t* drain = s_full + 8;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+  int* sBt = reinterpret_cast<int*>(smem + C::kOffBt);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split = blockIdx.x;
+  const int b = blockIdx.y / p.HKV;
+  const int hkv = blockIdx.y - b * p.HKV;
+
+  pdl_launch_dependents();  // the merge kernel may be scheduled now; it waits for this grid before reading
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kRing; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *sAbort = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tk);
+    prefetch_tensormap(&tv);
+  }
+  if (warp == 1) tmem_alloc(sTmem, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_wait();  // queries, cache, block table and lengths are written by earlier kernels
+  const int seq_len = __ldg(p.seq_lens + b);
+  int chunk, n_split;
+  sa_split(seq_len, p.max_splits, chunk, n_split);
+  const uint32_t tmem = *sTmem;
+  if (split < n_split) {
+    const int start = split * chunk;
+    const int end = min(start + chunk, max(seq_len, 0));
+    const int n_tiles = end > start ? (end - start + C::kTile - 1) / C::kTile : 0;
+    const int* bt = p.block_table + static_cast<int64_t>(b) * p.s_bt;
+    const int pg0 = start / p.page;
+    if (n_tiles > 0) {
+      const int npg = (end - 1) / p.page - pg0 + 1;
+      for (int i = threadIdx.x; i < npg && i < kSaBtCache; i += C::kThreads) sBt[i] = __ldg(bt + pg0 + i);
+    }
+    // the packed query rows (r = qi * G + gg) as the K-major A operand: per 64-column block, 64 rows x 128 B swizzled
+    uint8_t* sQ = smem + C::kOffQ;
+    const int hq0 = hkv * p.G;
+    for (int idx = threadIdx.x; idx < C::kRows * (D / 8); idx += C::kThreads) {
+      const int r = idx / (D / 8);
+      const int c = idx - r * (D / 8);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < p.R) {
+        const int qi = r / p.G;
+        v = *reinterpret_cast<const uint4*>(p.q + static_cast<int64_t>(b * p.Q + qi) * p.sq_t +
+                                            static_cast<int64_t>(hq0 + r - qi * p.G) * p.sq_h + c * 8);
+      }
+      *reinterpret_cast<uint4*>(sQ + sw_off(r, c, C::kRows * 128)) = v;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the query tile is read by the tensor cores
+    __syncthreads();
+
+    if (warp == 0) {
+      // ---------------------------------------------------------------------------------------- TMA producer
+      constexpr int kKBoxes = C::kKPieces * (C::kTile / 16);             // K: 16-token boxes per 64-column block
+      constexpr int kVBoxes = C::kVPieces * (C::kVTok / 16) * (D / 64);  // V: per 16-token box, every column block
+      static_assert(kKBoxes + kVBoxes <= 32, "one box per lane");
+      const uint64_t pol = policy_evict_first();
+      bool ok = true;
+      int issued = 0;  // tiles whose copies are all issued
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        const int base = start + C::kTile * i;
+        const int pc0 = i * C::kPiecesPerTile;
+        if (lane < C::kPiecesPerTile) {  // lane q2 arms piece q2 of the tile: its slot, then its byte count
+          const int q2 = lane;
+          const int pc = pc0 + q2;
+          const int slot = pc % C::kRing;
+          if (pc >= C::kRing && !sa_wait(&empty[slot], ((pc / C::kRing) - 1) & 1, sAbort)) {
+            sa_abort(p, sAbort);
+            ok = false;
+          } else {
+            int nb;  // bytes of the piece below `end`
+            if (q2 < C::kKPieces) {
+              nb = min(C::kTile / 16, (end - base + 15) / 16) * 2048;
+            } else {
+              const int t0 = base + (q2 - C::kKPieces) * C::kVTok;
+              nb = (t0 < end ? min(C::kVTok / 16, (end - t0 + 15) / 16) : 0) * (D / 64) * 2048;
+            }
+            mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nb));
+          }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        if (lane < kKBoxes + kVBoxes) {  // lane l issues one box of the tile
+          int q2, pos, col, off_b;
+          if (lane < kKBoxes) {  // K: piece = column block, box = 16 tokens of the tile
+            q2 = lane / (C::kTile / 16);
+            const int g = lane - q2 * (C::kTile / 16);
+            pos = base + 16 * g;
+            col = 64 * q2;
+            off_b = g * 2048;
+          } else {               // V: piece = kVTok tokens, box = (16 tokens, column block)
+            const int l2 = lane - kKBoxes;
+            const int per = (C::kVTok / 16) * (D / 64);
+            const int v = l2 / per;
+            const int g = (l2 - v * per) / (D / 64);
+            const int j = l2 - v * per - g * (D / 64);
+            q2 = C::kKPieces + v;
+            pos = base + v * C::kVTok + 16 * g;
+            col = 64 * j;
+            off_b = j * C::kVLbo + g * 2048;
+          }
+          if (pos < end) {
+            const int slot = (pc0 + q2) % C::kRing;
+            const int pg = pos / p.page;
+            const int blk = pg - pg0 < kSaBtCache ? sBt[pg - pg0] : __ldg(bt + pg);
+            const int off = pos - pg * p.page;
+            tma_load_4d(smem + slot * C::kPiece + off_b, lane < kKBoxes ? &tk : &tv, &full[slot], col,
+                        p.head_inner ? hkv : off, p.head_inner ? off : hkv, blk, pol);
+          }
+        }
+        issued = i + 1;
+      }
+      if (*sAbort && lane == 0) {  // let the issued copies of the last pieces land (one bounded wait in all)
+        const int pcn = issued * C::kPiecesPerTile;
+        const uint64_t t0 = global_timer_ns();
+        for (int q2 = pcn > C::kRing ? pcn - C::kRing : 0; q2 < pcn; ++q2) {
+          while (!mbar_try_wait(&full[q2 % C::kRing], (q2 / C::kRing) & 1) && global_timer_ns() - t0 < kSaWaitNs) {
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = idesc_bf16(C::kRows, C::kTile, false, false);
+        constexpr uint32_t idesc_o = idesc_bf16(C::kRows, D, false, true);
+        const uint32_t sm_base = smem_u32(smem);
+        const uint32_t q_base = smem_u32(sQ);
+        const uint32_t p_base = smem_u32(smem + C::kOffP);
+        bool ok = true;
+        // pieces are numbered in the producer's order (tile i: its K pieces, then its V pieces); the scores of tile
+        // i + 1 consume K pieces before the V pieces of tile i
+        auto wait_piece = [&](int pc, int& slot) -> bool {
+          slot = pc % C::kRing;
+          if (!sa_wait(&full[slot], (pc / C::kRing) & 1, sAbort)) {
+            sa_abort(p, sAbort);
+            return false;
+          }
+          tc_fence_after();
+          return true;
+        };
+        auto issue_s = [&](int i) -> bool {
+          const int sb = i & 1;
+          if (i >= 2 && !sa_wait(&s_free[sb], ((i >> 1) - 1) & 1, sAbort)) {
+            sa_abort(p, sAbort);
+            return false;
+          }
+          tc_fence_after();
+          for (int j = 0; j < C::kKPieces; ++j) {
+            int slot;
+            if (!wait_piece(i * C::kPiecesPerTile + j, slot)) return false;
+            const uint32_t a0 = q_base + j * C::kRows * 128;
+            const uint32_t b0 = sm_base + slot * C::kPiece;
+#pragma unroll
+            for (int s2 = 0; s2 < 4; ++s2)
+              mma_bf16_ss(tmem + C::kColS + sb * C::kTile, smem_desc_k128_sw128(a0 + 32 * s2),
+                          smem_desc_k128_sw128(b0 + 32 * s2), idesc_s, (j | s2) != 0);
+            mma_commit(&empty[slot]);
+          }
+          mma_commit(&s_full[sb]);
+          return true;
+        };
+        auto issue_pv = [&](int i) -> bool {
+          const int sb = i & 1;
+          if (!sa_wait(&p_full[sb], (i >> 1) & 1, sAbort)) {
+            sa_abort(p, sAbort);
+            return false;
+          }
+          tc_fence_after();
+          const int base = start + C::kTile * i;
+          for (int v = 0; v < C::kVPieces; ++v) {
+            int slot;
+            if (!wait_piece(i * C::kPiecesPerTile + C::kKPieces + v, slot)) return false;
+            const uint32_t b0 = sm_base + slot * C::kPiece;
+#pragma unroll
+            for (int s2 = 0; s2 < C::kVTok / 16; ++s2) {
+              const int tk0 = v * C::kVTok + 16 * s2;  // token of the k-step within the tile
+              if (base + tk0 >= end) continue;       // past the chunk: no keys, no copies
+              mma_bf16_ss(tmem + C::kColO, smem_desc_k128_sw128(p_base + sb * C::kPBytes + (tk0 >> 4) * 32),
+                          smem_desc_mn_sw128(b0 + s2 * 2048, C::kVLbo, 1024), idesc_o, (i | tk0) != 0);
+            }
+            mma_commit(&empty[slot]);
+          }
+          mma_commit(&pv_done[sb]);
+          return true;
+        };
+        if (n_tiles > 0) ok = issue_s(0);
+        for (int i = 0; i < n_tiles && ok; ++i) {
+          if (i + 1 < n_tiles) ok = issue_s(i + 1);
+          if (ok) ok = issue_pv(i);
+        }
+        // every issued MMA has completed before the roles finish (and tensor memory is freed)
+        mma_commit(drain);
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kSaWaitNs) {
+        }
+      }
+    } else {
+      // ---------------------------------------------------------------------------------------- softmax warps
+      // lanes 0-15 of warp w own packed row r = 16 (w % 4) + lane (tensor-memory lane 32 (w % 4) + lane)
+      const int q4 = warp & 3;
+      const bool row_lane = lane < 16;
+      const int r = 16 * q4 + (lane & 15);
+      const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
+      uint8_t* prow = smem + C::kOffP + r * 128;  // this row of P (slot 0)
+      const bool live = row_lane && r < p.R;
+      const int lim = seq_len - p.Q + (live ? r / p.G : 0);  // the row sees keys <= lim
+      float m_run = -INFINITY;  // reference maximum (base 2)
+      float l_run = 0.f;        // sum of 2^(s - m_run)
+      bool ok = true;
+      // every wait's outcome is made warp-uniform: tcgen05.ld / st are warp-collective
+      auto wait_or_abort = [&](uint64_t* bar, uint32_t parity) -> bool {
+        bool got = sa_wait(bar, parity, sAbort);
+        if (!got) sa_abort(p, sAbort);
+        return __all_sync(0xffffffffu, got);
+      };
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        const int sb = i & 1;
+        const int base = start + C::kTile * i;
+        if (!(ok = wait_or_abort(&s_full[sb], (i >> 1) & 1))) break;
+        tc_fence_after();
+        float x[C::kTile];
+#pragma unroll
+        for (int g2 = 0; g2 < C::kTile / 32; ++g2) {
+          uint32_t r32[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + C::kColS + sb * C::kTile + 32 * g2, r32);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) x[32 * g2 + j] = __uint_as_float(r32[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);
+        // base-2 scaled scores; keys past the chunk's end or the row's causal limit are -inf
+        const int kmax = min(end, lim + 1) - base;  // tokens [0, kmax) of the tile are keys of this row
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < C::kTile; ++t) {
+          x[t] = (live && t < kmax) ? x[t] * p.qk_scale : -INFINITY;
+          tmax = fmaxf(tmax, x[t]);
+        }
+        // raise the reference only when the row's maximum grows by more than 2^8 (or first appears): P stays below 2^8
+        const bool want = tmax > m_run + 8.f || (m_run == -INFINITY && tmax > -INFINITY);
+        float al = 1.f;
+        if (want) {
+          const float mn = fmaxf(m_run, tmax);
+          al = m_run == -INFINITY ? 0.f : ex2_approx(m_run - mn);
+          l_run *= al;
+          m_run = mn;
+        }
+        if (i > 0 && __any_sync(0xffffffffu, want)) {
+          // O holds P V of the earlier tiles: scale the raised rows (factor 1 for the others) once the last P V landed
+          if (!(ok = wait_or_abort(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1))) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r32[32];
+            const uint32_t ta = tmem + lane_off + C::kColO + 32 * c;
+            tmem_ld_32x32b_x32(ta, r32);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r32[j] = __float_as_uint(__uint_as_float(r32[j]) * al);
+            tmem_st_32x32b_x32(ta, r32);
+          }
+          tc_fence_before();
+        }
+        // P = 2^(x - m) in bf16 as this row of the A operand in slot sb (free once P V of tile i - 2 has completed)
+        if (i >= 2 && !(ok = wait_or_abort(&pv_done[sb], ((i >> 1) - 1) & 1))) break;
+        const float mu = m_run == -INFINITY ? 0.f : m_run;
+        float ls = 0.f;
+        uint32_t pk[C::kTile / 2];
+#pragma unroll
+        for (int t = 0; t < C::kTile; t += 2) {
+          const float p0 = ex2_approx(x[t] - mu);
+          const float p1 = ex2_approx(x[t + 1] - mu);
+          ls += p0 + p1;
+          pk[t / 2] = pack_bf16x2(p0, p1);
+        }
+        l_run += ls;
+        if (row_lane) {
+          uint8_t* dst = prow + sb * C::kPBytes;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        }
+        // slots past the chunk's end inside a 16-token step that still has keys were copied from their page (maybe
+        // never written): zero their V rows so that P = 0 cannot meet a NaN
+        const int kend = end - base;  // tokens [kend, 16 * ceil(kend / 16)) of the tile
+        if (kend < C::kTile && (kend & 15)) {
+          const int st0 = kend & ~15;
+          const int vv = st0 / C::kVTok;
+          const int pcv = i * C::kPiecesPerTile + C::kKPieces + vv;
+          if (!(ok = wait_or_abort(&full[pcv % C::kRing], (pcv / C::kRing) & 1))) break;
+          const int nz = (16 - (kend & 15)) * (D / 64) * 8;  // 16-byte words to clear
+          for (int idx = 32 * (warp - 2) + lane; idx < nz; idx += 128) {
+            const int w16 = idx & 7;
+            const int rest = idx >> 3;
+            const int j = rest % (D / 64);
+            const int t = kend + rest / (D / 64);
+            *reinterpret_cast<uint4*>(smem + (pcv % C::kRing) * C::kPiece + j * C::kVLbo + (t - vv * C::kVTok) * 128 +
+                                      16 * w16) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P (and zeroed V) for the tensor cores
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[sb]);
+      }
+      if (ok && n_tiles > 0 && wait_or_abort(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1)) {
+        // O / l for this row (D columns of its tensor-memory lane)
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        const bool single = n_split == 1;
+        const int64_t part_row0 = (static_cast<int64_t>(b * p.HKV + hkv) * p.max_splits + split) * p.R;
+        const int qi = live ? r / p.G : 0;
+        __nv_bfloat16* orow =
+            p.out + static_cast<int64_t>(b * p.Q + qi) * p.so_t + static_cast<int64_t>(hq0 + r - qi * p.G) * p.so_h;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r32[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + C::kColO + 32 * c, r32);
+          if (live) {
+            if (single) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8)
+                *reinterpret_cast<uint4*>(orow + 32 * c + j) =
+                    make_uint4(pack_bf16x2(__uint_as_float(r32[j]) * inv, __uint_as_float(r32[j + 1]) * inv),
+                               pack_bf16x2(__uint_as_float(r32[j + 2]) * inv, __uint_as_float(r32[j + 3]) * inv),
+                               pack_bf16x2(__uint_as_float(r32[j + 4]) * inv, __uint_as_float(r32[j + 5]) * inv),
+                               pack_bf16x2(__uint_as_float(r32[j + 6]) * inv, __uint_as_float(r32[j + 7]) * inv));
+            } else {
+              float* prt = p.o_part + (part_row0 + r) * D + 32 * c;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(prt + j) =
+                    make_float4(__uint_as_float(r32[j]) * inv, __uint_as_float(r32[j + 1]) * inv,
+                                __uint_as_float(r32[j + 2]) * inv, __uint_as_float(r32[j + 3]) * inv);
+            }
+          }
+        }
+        if (live && !single) p.lse_part[part_row0 + r] = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
+      } else if (ok && n_tiles == 0 && n_split == 1 && live) {
+        // no key at all (seq_len <= 0): zeros
+        const int qi = r / p.G;
+        __nv_bfloat16* orow =
+            p.out + static_cast<int64_t>(b * p.Q + qi) * p.so_t + static_cast<int64_t>(hq0 + r - qi * p.G) * p.so_h;
+        for (int d = 0; d < D; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
 // ----------------------------------------------------------------------------------------------- host side
 std::mutex g_sa_mu;
 int g_sa_sms[64] = {};
@@ -614,6 +1056,23 @@ int sa_encode(CUtensorMap* map, const void* base, int D, int page, int hkv, int 
   return QF_OK;
 }
 
+// The merge launch shared by both attention kernels (skipped when every request has one split).
+template <int D>
+int sa_launch_merge(const SaParams& p, int num_reqs, cudaStream_t st) {
+  if (p.max_splits == 1) return QF_OK;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t mc = {};
+  mc.gridDim = dim3(static_cast<unsigned>(num_reqs * p.HKV * p.R));
+  mc.blockDim = dim3(256);
+  mc.stream = st;
+  mc.attrs = attr;
+  mc.numAttrs = 1;  // scheduled behind the attention grid; reads its outputs after griddepcontrol.wait
+  const cudaError_t e = cudaLaunchKernelEx(&mc, spec_attn_merge_kernel<D>, p);
+  return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, std::string("merge launch: ") + cudaGetErrorString(e));
+}
+
 template <int D, int MT>
 int sa_launch(const CUtensorMap& tk, const CUtensorMap& tv, const SaParams& p, int num_reqs, int dev, unsigned flags,
               cudaStream_t st) {
@@ -640,16 +1099,47 @@ int sa_launch(const CUtensorMap& tk, const CUtensorMap& tv, const SaParams& p, i
   cfg.numAttrs = (flags & QF_FLAG_PDL) ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, spec_attn_kernel<D, MT>, tk, tv, p);
   if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("attention launch: ") + cudaGetErrorString(e));
-  if (p.max_splits == 1) return QF_OK;  // every request has one split: outputs written
-  const int rows = num_reqs * p.HKV * p.R;
-  cudaLaunchConfig_t mc = {};
-  mc.gridDim = dim3(static_cast<unsigned>(rows));
-  mc.blockDim = dim3(256);
-  mc.stream = st;
-  mc.attrs = attr;
-  mc.numAttrs = 1;  // scheduled behind the attention grid; reads its outputs after griddepcontrol.wait
-  e = cudaLaunchKernelEx(&mc, spec_attn_merge_kernel<D>, p);
-  return e == cudaSuccess ? QF_OK : fail(QF_ERR_LAUNCH, std::string("merge launch: ") + cudaGetErrorString(e));
+  return sa_launch_merge<D>(p, num_reqs, st);
+}
+
+template <int D>
+int sa_launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const SaParams& p, int num_reqs, int dev,
+                 unsigned flags, cudaStream_t st) {
+  using C = SaTcGeo<D>;
+  static bool attr_set[64] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_sa_mu);
+    if (!attr_set[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(spec_attn_tc_kernel<D>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+      if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      attr_set[dev] = true;
+    }
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.max_splits), static_cast<unsigned>(num_reqs * p.HKV));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & QF_FLAG_PDL) ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, spec_attn_tc_kernel<D>, tk, tv, p);
+  if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("attention launch: ") + cudaGetErrorString(e));
+  return sa_launch_merge<D>(p, num_reqs, st);
+}
+
+// QF_ATTN_MMA_SYNC=1 (read only with QF_TEST_OVERRIDES=1) keeps head sizes 128 / 256 on the mma.sync kernel, so
+// that tests can run both kernels on the same shapes.
+bool force_mma_sync() {
+  static const bool on = [] {
+    const char* t = std::getenv("QF_TEST_OVERRIDES");
+    const char* v = std::getenv("QF_ATTN_MMA_SYNC");
+    return t && std::strcmp(t, "1") == 0 && v && std::strcmp(v, "1") == 0;
+  }();
+  return on;
 }
 
 template <int D>
@@ -742,6 +1232,10 @@ int qf_spec_attn(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache,
   p.qk_scale = scale * 1.4426950408889634f;
   const int MT = static_cast<int>((R + 15) / 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_size >= 128 && !force_mma_sync()) {  // tensor-core (tcgen05) kernel
+    if (head_size == 256) return sa_launch_tc<256>(tk, tv, p, num_reqs, dev, flags, st);
+    return sa_launch_tc<128>(tk, tv, p, num_reqs, dev, flags, st);
+  }
   if (head_size == 256) return sa_dispatch_mt<256>(MT, tk, tv, p, num_reqs, dev, flags, st);
   if (head_size == 128) return sa_dispatch_mt<128>(MT, tk, tv, p, num_reqs, dev, flags, st);
   return sa_dispatch_mt<64>(MT, tk, tv, p, num_reqs, dev, flags, st);

@@ -13,6 +13,7 @@ Shapes: the reference's test matrix (bench/test_spec_attn.py: H = 24, HKV = 4, D
 [2, blocks, page, HKV, D] cache layout (slot stride > head stride), 16-slot pages, head sizes 64 / 128, one to four
 16-row m-tiles (Q * G up to 64), several requests of different lengths with a zero-length one, CUDA-graph replay
 with lengths changed in place, and the on-box reference Triton kernel when it is installed under baseline/_ref.
+Head sizes 128 / 256 take the tcgen05 kernel; the last test reruns part of the file on the mma.sync kernel.
 """
 from __future__ import annotations
 
@@ -211,3 +212,16 @@ def test_matches_reference_triton_on_box(dev, ctx, Q, B):
     torch.cuda.synchronize(dev)
     theirs = bf16_to_f32(from_dev_bf16(out)).astype(np.float64)
     assert np.linalg.norm(bf16_to_f32(got) - theirs) / np.linalg.norm(theirs) <= 5e-3
+
+
+def test_mma_sync_kernel_on_the_same_shapes(dev):
+    """Head sizes 128 / 256 run on the tcgen05 kernel by default; the mma.sync kernel (which serves head size 64) is
+    forced for them in a child process (QF_ATTN_MMA_SYNC=1 with QF_TEST_OVERRIDES=1, read once per process) and held
+    to the same bars on the golden cases and part of the reference matrix."""
+    import os
+    import subprocess
+    env = dict(os.environ, QF_TEST_OVERRIDES="1", QF_ATTN_MMA_SYNC="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        "tests/test_gpu_spec_attn.py", "-k", "golden or (reference_matrix and 8000) or vllm_layout"],
+                       cwd=REPO, capture_output=True, text=True, timeout=900, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
