@@ -494,6 +494,8 @@ __global__ void __launch_bounds__(256) spec_attn_merge_kernel(const SaParams p) 
   __shared__ float sW[kSaMaxSplits];
   __shared__ float sRed[8];
   __shared__ float4 sAcc[NG][NQ];
+  pdl_launch_dependents();  // the next kernel's prologue may overlap this one; it reads nothing written here before
+                            // its own griddepcontrol.wait
   pdl_wait();  // the partial outputs of spec_attn_kernel
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
@@ -580,24 +582,28 @@ __global__ void __launch_bounds__(256) spec_attn_merge_kernel(const SaParams p) 
 // thread's row from tcgen05.ld, a reference maximum raised only when the row's maximum grows by more than 2^8 (then
 // the row's O and sum are rescaled in place), P rounded to bf16 and stored as the row of the A operand, and at the end
 // O / l written as outputs or split partials like the mma.sync kernel.
-template <int D> struct SaTcGeo {
+template <int D, int RP> struct SaTcGeo {
   static constexpr int kThreads = 192;
   static constexpr int kTile = 64;                   // tokens per tile
   static constexpr int kRows = 64;                   // M of both products
+  // Only RP (32 or 64) rows of the query tile and of P are stored: with RP = 32 the M = 64 operands read their rows
+  // 32-63 from the memory that follows (the next 64-column block, the other P buffer, or the pad below), which only
+  // feeds accumulator rows that are never output.
   static constexpr int kPiece = 8192;
   static constexpr int kKPieces = D / 64;            // K: [64 tokens][64 columns] per piece
   static constexpr int kVTok = kPiece / (2 * D);     // V: tokens per piece, all D columns
   static constexpr int kVPieces = kTile / kVTok;
   static constexpr int kPiecesPerTile = kKPieces + kVPieces;
   static constexpr int kVLbo = kVTok * 128;          // V piece: 64-column blocks of kVTok 128-byte rows
-  static constexpr int kQBytes = (D / 64) * kRows * 128;
-  static constexpr int kPBytes = kRows * 128;        // P: [64 rows][64 tokens x 2 B]
+  static constexpr int kQBytes = (D / 64) * RP * 128;
+  static constexpr int kPBytes = RP * 128;           // P: [RP rows][64 tokens x 2 B]
+  static constexpr int kPad = (kRows - RP) * 128;    // readable bytes after the last operand block
   static constexpr int kMiscBytes = 4 * kSaBtCache + 1024;
-  static constexpr int kRingFit = (227 * 1024 - kQBytes - 2 * kPBytes - kMiscBytes - 1024) / kPiece;
+  static constexpr int kRingFit = (227 * 1024 - kQBytes - 2 * kPBytes - kPad - kMiscBytes - 1024) / kPiece;
   static constexpr int kRing = kRingFit > 32 ? 32 : kRingFit;
   static constexpr int kOffQ = kRing * kPiece;
   static constexpr int kOffP = kOffQ + kQBytes;
-  static constexpr int kOffBt = kOffP + 2 * kPBytes;
+  static constexpr int kOffBt = kOffP + 2 * kPBytes + kPad;
   static constexpr int kOffBar = kOffBt + 4 * kSaBtCache;
   // barriers: full[kRing], empty[kRing], s_full[2], s_free[2], p_full[2], pv_done[2], drain
   static constexpr int kNumBars = 2 * kRing + 9;
@@ -609,13 +615,14 @@ template <int D> struct SaTcGeo {
   static_assert(kRing >= 2 * kPiecesPerTile, "ring shallower than two tiles");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
   static_assert(D == 128 || D == 256, "tcgen05 path head sizes");
+  static_assert(RP == 32 || RP == 64, "stored rows");
 };
 
-template <int D>
+template <int D, int RP>
 __global__ void __launch_bounds__(192, 1)
     spec_attn_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                         const SaParams p) {
-  using C = SaTcGeo<D>;
+  using C = SaTcGeo<D, RP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
@@ -672,10 +679,10 @@ __global__ void __launch_bounds__(192, 1)
       const int npg = (end - 1) / p.page - pg0 + 1;
       for (int i = threadIdx.x; i < npg && i < kSaBtCache; i += C::kThreads) sBt[i] = __ldg(bt + pg0 + i);
     }
-    // the packed query rows (r = qi * G + gg) as the K-major A operand: per 64-column block, 64 rows x 128 B swizzled
+    // the packed query rows (r = qi * G + gg) as the K-major A operand: per 64-column block, RP rows x 128 B swizzled
     uint8_t* sQ = smem + C::kOffQ;
     const int hq0 = hkv * p.G;
-    for (int idx = threadIdx.x; idx < C::kRows * (D / 8); idx += C::kThreads) {
+    for (int idx = threadIdx.x; idx < RP * (D / 8); idx += C::kThreads) {
       const int r = idx / (D / 8);
       const int c = idx - r * (D / 8);
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -684,7 +691,7 @@ __global__ void __launch_bounds__(192, 1)
         v = *reinterpret_cast<const uint4*>(p.q + static_cast<int64_t>(b * p.Q + qi) * p.sq_t +
                                             static_cast<int64_t>(hq0 + r - qi * p.G) * p.sq_h + c * 8);
       }
-      *reinterpret_cast<uint4*>(sQ + sw_off(r, c, C::kRows * 128)) = v;
+      *reinterpret_cast<uint4*>(sQ + sw_off(r, c, RP * 128)) = v;
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the query tile is read by the tensor cores
     __syncthreads();
@@ -788,7 +795,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int j = 0; j < C::kKPieces; ++j) {
             int slot;
             if (!wait_piece(i * C::kPiecesPerTile + j, slot)) return false;
-            const uint32_t a0 = q_base + j * C::kRows * 128;
+            const uint32_t a0 = q_base + j * RP * 128;
             const uint32_t b0 = sm_base + slot * C::kPiece;
 #pragma unroll
             for (int s2 = 0; s2 < 4; ++s2)
@@ -871,12 +878,16 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) mbar_arrive(&s_free[sb]);
         // base-2 scaled scores; keys past the chunk's end or the row's causal limit are -inf
         const int kmax = min(end, lim + 1) - base;  // tokens [0, kmax) of the tile are keys of this row
-        float tmax = -INFINITY;
 #pragma unroll
-        for (int t = 0; t < C::kTile; ++t) {
-          x[t] = (live && t < kmax) ? x[t] * p.qk_scale : -INFINITY;
-          tmax = fmaxf(tmax, x[t]);
-        }
+        for (int t = 0; t < C::kTile; ++t) x[t] = (live && t < kmax) ? x[t] * p.qk_scale : -INFINITY;
+        float mx[16];  // the row maximum as a tree (independent chains)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) mx[j] = fmaxf(fmaxf(x[j], x[j + 16]), fmaxf(x[j + 32], x[j + 48]));
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) mx[j] = fmaxf(mx[j], mx[j + w]);
+        const float tmax = mx[0];
         // raise the reference only when the row's maximum grows by more than 2^8 (or first appears): P stays below 2^8
         const bool want = tmax > m_run + 8.f || (m_run == -INFINITY && tmax > -INFINITY);
         float al = 1.f;
@@ -904,17 +915,19 @@ __global__ void __launch_bounds__(192, 1)
         // P = 2^(x - m) in bf16 as this row of the A operand in slot sb (free once P V of tile i - 2 has completed)
         if (i >= 2 && !(ok = wait_or_abort(&pv_done[sb], ((i >> 1) - 1) & 1))) break;
         const float mu = m_run == -INFINITY ? 0.f : m_run;
-        float ls = 0.f;
+        float ls[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ls[j] = 0.f;
         uint32_t pk[C::kTile / 2];
 #pragma unroll
         for (int t = 0; t < C::kTile; t += 2) {
           const float p0 = ex2_approx(x[t] - mu);
           const float p1 = ex2_approx(x[t + 1] - mu);
-          ls += p0 + p1;
+          ls[(t >> 1) & 7] += p0 + p1;
           pk[t / 2] = pack_bf16x2(p0, p1);
         }
-        l_run += ls;
-        if (row_lane) {
+        l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+        if (row_lane && r < RP) {
           uint8_t* dst = prow + sb * C::kPBytes;
 #pragma unroll
           for (int c = 0; c < 8; ++c)
@@ -1102,15 +1115,15 @@ int sa_launch(const CUtensorMap& tk, const CUtensorMap& tv, const SaParams& p, i
   return sa_launch_merge<D>(p, num_reqs, st);
 }
 
-template <int D>
+template <int D, int RP>
 int sa_launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const SaParams& p, int num_reqs, int dev,
                  unsigned flags, cudaStream_t st) {
-  using C = SaTcGeo<D>;
+  using C = SaTcGeo<D, RP>;
   static bool attr_set[64] = {};
   {
     std::lock_guard<std::mutex> lk(g_sa_mu);
     if (!attr_set[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(spec_attn_tc_kernel<D>,
+      const cudaError_t e = cudaFuncSetAttribute(spec_attn_tc_kernel<D, RP>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
       if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
       attr_set[dev] = true;
@@ -1126,7 +1139,7 @@ int sa_launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const SaParams& p
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = (flags & QF_FLAG_PDL) ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, spec_attn_tc_kernel<D>, tk, tv, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, spec_attn_tc_kernel<D, RP>, tk, tv, p);
   if (e != cudaSuccess) return fail(QF_ERR_LAUNCH, std::string("attention launch: ") + cudaGetErrorString(e));
   return sa_launch_merge<D>(p, num_reqs, st);
 }
@@ -1233,8 +1246,11 @@ int qf_spec_attn(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache,
   const int MT = static_cast<int>((R + 15) / 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_size >= 128 && !force_mma_sync()) {  // tensor-core (tcgen05) kernel
-    if (head_size == 256) return sa_launch_tc<256>(tk, tv, p, num_reqs, dev, flags, st);
-    return sa_launch_tc<128>(tk, tv, p, num_reqs, dev, flags, st);
+    if (head_size == 256)
+      return R <= 32 ? sa_launch_tc<256, 32>(tk, tv, p, num_reqs, dev, flags, st)
+                     : sa_launch_tc<256, 64>(tk, tv, p, num_reqs, dev, flags, st);
+    return R <= 32 ? sa_launch_tc<128, 32>(tk, tv, p, num_reqs, dev, flags, st)
+                   : sa_launch_tc<128, 64>(tk, tv, p, num_reqs, dev, flags, st);
   }
   if (head_size == 256) return sa_dispatch_mt<256>(MT, tk, tv, p, num_reqs, dev, flags, st);
   if (head_size == 128) return sa_dispatch_mt<128>(MT, tk, tv, p, num_reqs, dev, flags, st);
