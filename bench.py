@@ -65,6 +65,7 @@ def parse_args():
                          "the standalone NVLink one-shot kernel, or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-attn", action="store_true", help="skip the verification-attention figure added to the line")
     ap.add_argument("--sweep", action="store_true", help="per-shape table (config 4) instead of the step")
     ap.add_argument("--sweep-out", default="")
     ap.add_argument("--ref-triton", action="store_true", help="with --sweep: also time the reference's own Triton "
@@ -493,6 +494,9 @@ def run_ours(args, rank: int, world: int, local: int):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_sample(args.m)
+    attn = None
+    if rank == 0 and world == 1 and not args.no_attn:
+        attn = measure_spec_attn(dev, stream)
 
     from qwen_a100_fastpath_b200.w8a16 import workspace_status
     status = workspace_status(dev, stream)
@@ -523,8 +527,49 @@ def run_ours(args, rank: int, world: int, local: int):
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
             "gpu_launches": st.launches_per_step * args.steps,
             "step_floor_ms_at_measured_peak": round(st.bytes_rank / (peak_hbm()[0] * 1e9) * 1e3, 4),
-            "device_error_flag": status}
+            "device_error_flag": status,
+            "spec_attn": attn}
     print(json.dumps(line), flush=True)
+
+
+def measure_spec_attn(dev, stream, ctx: int = 38000):
+    """The verification attention (QWEN_FAST_ATTN row) on the reference's attention shape at one context: one request,
+    Q = 3, 24 query / 4 KV heads, head size 256, 800-slot pages; a CUDA graph of launches over three distinct KV caches
+    (together above L2).  Reported beside the step, not part of it."""
+    import torch
+    from qwen_a100_fastpath_b200.spec_attn import gqa_packed_spec_attention, workspace_status
+    H, HKV, D, page, Q = 24, 4, 256, 800, 3
+    L = ctx + Q
+    pages = (L + page - 1) // page
+    g = torch.Generator(device=dev).manual_seed(17)
+    caches = []
+    for _ in range(3):
+        kv = torch.randn(pages + 1, HKV, page, 2 * D, device=dev, generator=g).to(torch.bfloat16)
+        bt = torch.randperm(pages + 1, device=dev, generator=g)[:pages].to(torch.int32).view(1, pages)
+        caches.append((kv, *kv.transpose(1, 2).split(D, dim=-1), bt))
+    q = torch.randn(Q, H, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    lens = torch.tensor([L], dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        for c in caches:
+            gqa_packed_spec_attention(q, c[1], c[2], out, lens, c[3], 1, Q, HKV, D ** -0.5)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        for _ in range(8):
+            for c in caches:
+                gqa_packed_spec_attention(q, c[1], c[2], out, lens, c[3], 1, Q, HKV, D ** -0.5)
+    us = time_graph(gr, stream, 5, 3) / 24 * 1e3
+    del gr
+    kv_bytes = L * HKV * 2 * D * 2
+    peak, _ = peak_hbm()
+    res = {"ctx": ctx, "q_len": Q, "heads": H, "kv_heads": HKV, "head_size": D, "page": page, "us": round(us, 2),
+           "kv_GBps": round(kv_bytes / us / 1e3, 1), "frac_of_measured_hbm": round(kv_bytes / us / 1e3 / peak, 3),
+           "kernel": "spec_attn_tc_kernel<256, 32> + spec_attn_merge_kernel (tcgen05)",
+           "status": workspace_status(dev)}
+    del caches
+    torch.cuda.empty_cache()
+    return res
 
 
 def load_reference_triton():
