@@ -574,16 +574,17 @@ __global__ void __launch_bounds__(256) spec_attn_merge_kernel(const SaParams p) 
 // An M = 64 accumulator puts row r in tensor-memory lane r % 16 + 32 (r / 16): lanes 0-15 of each of the four softmax
 // warps own a row each, so a row's maximum, exponentials and sum are thread-local (no shuffles, no exchange between
 // warps).  The padding rows cost tensor-core time only, which the kernel has to spare (the MMAs are a few percent of
-// it).  Roles (6 warps): warp 0 streams K and V with TMA into a ring of 8 KiB pieces (K: one 64-column block of the
+// it).  Roles (7 warps): warp 0 streams K and V with TMA into a ring of 8 KiB pieces (K: one 64-column block of the
 // tile's 64 tokens; V: 16 (D = 256) or 32 (D = 128) tokens of every column) -- lane q arms piece q of the tile, then
-// every lane issues one 16-token box, since one issuing thread caps the copy rate well below HBM bandwidth; warp 1
-// allocates tensor memory and lane 0 issues the MMAs (S of tile i + 1 before P V of tile i, so the softmax of tile i
-// overlaps the next scores) and releases pieces with tcgen05.commit; warps 2-5 are the softmax: base-2 scores of the
+// every lane issues one 16-token box, since one issuing thread caps the copy rate well below HBM bandwidth; it starts
+// as soon as the barriers exist, while warps 1-6 load the query tile; warp 1 allocates tensor memory and its lane 0
+// issues the score MMAs, warp 6 lane 0 the value MMAs (two S buffers: the scores of tile i + 1 run while the softmax
+// of tile i does), each releasing pieces with tcgen05.commit; warps 2-5 are the softmax: base-2 scores of the
 // thread's row from tcgen05.ld, a reference maximum raised only when the row's maximum grows by more than 2^8 (then
 // the row's O and sum are rescaled in place), P rounded to bf16 and stored as the row of the A operand, and at the end
 // O / l written as outputs or split partials like the mma.sync kernel.
 template <int D, int RP> struct SaTcGeo {
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 224;
   static constexpr int kTile = 64;                   // tokens per tile
   static constexpr int kRows = 64;                   // M of both products
   // Only RP (32 or 64) rows of the query tile and of P are stored: with RP = 32 the M = 64 operands read their rows
@@ -605,8 +606,8 @@ template <int D, int RP> struct SaTcGeo {
   static constexpr int kOffP = kOffQ + kQBytes;
   static constexpr int kOffBt = kOffP + 2 * kPBytes + kPad;
   static constexpr int kOffBar = kOffBt + 4 * kSaBtCache;
-  // barriers: full[kRing], empty[kRing], s_full[2], s_free[2], p_full[2], pv_done[2], drain
-  static constexpr int kNumBars = 2 * kRing + 9;
+  // barriers: full[kRing], empty[kRing], s_full[2], s_free[2], p_full[2], pv_done[2], drain, q_ready
+  static constexpr int kNumBars = 2 * kRing + 10;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;             // tensor-memory address, abort flag
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;
   static constexpr uint32_t kColS = 0;                               // S buffers b at b * 64
@@ -619,7 +620,7 @@ template <int D, int RP> struct SaTcGeo {
 };
 
 template <int D, int RP>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(224, 1)
     spec_attn_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                         const SaParams p) {
   using C = SaTcGeo<D, RP>;
@@ -633,6 +634,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* p_full = s_full + 4;
   uint64_t* pv_done = s_full + 6;
   uint64_t* drain = s_full + 8;
+  uint64_t* q_ready = s_full + 9;  // the query tile is in shared memory (one arrival per loading warp)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
   int* sBt = reinterpret_cast<int*>(smem + C::kOffBt);
@@ -654,7 +656,8 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);  // one commit from each MMA lane
+    mbar_init(q_ready, C::kThreads / 32 - 1);
     *sAbort = 0;
     fence_mbar_init();
     prefetch_tensormap(&tk);
@@ -675,26 +678,33 @@ __global__ void __launch_bounds__(192, 1)
     const int n_tiles = end > start ? (end - start + C::kTile - 1) / C::kTile : 0;
     const int* bt = p.block_table + static_cast<int64_t>(b) * p.s_bt;
     const int pg0 = start / p.page;
-    if (n_tiles > 0) {
-      const int npg = (end - 1) / p.page - pg0 + 1;
-      for (int i = threadIdx.x; i < npg && i < kSaBtCache; i += C::kThreads) sBt[i] = __ldg(bt + pg0 + i);
-    }
-    // the packed query rows (r = qi * G + gg) as the K-major A operand: per 64-column block, RP rows x 128 B swizzled
     uint8_t* sQ = smem + C::kOffQ;
     const int hq0 = hkv * p.G;
-    for (int idx = threadIdx.x; idx < RP * (D / 8); idx += C::kThreads) {
-      const int r = idx / (D / 8);
-      const int c = idx - r * (D / 8);
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r < p.R) {
-        const int qi = r / p.G;
-        v = *reinterpret_cast<const uint4*>(p.q + static_cast<int64_t>(b * p.Q + qi) * p.sq_t +
-                                            static_cast<int64_t>(hq0 + r - qi * p.G) * p.sq_h + c * 8);
+    if (warp == 0) {
+      // the chunk's pages for the producer only (no CTA barrier: the copies start while the others load the queries)
+      if (n_tiles > 0) {
+        const int npg = (end - 1) / p.page - pg0 + 1;
+        for (int i = lane; i < npg && i < kSaBtCache; i += 32) sBt[i] = __ldg(bt + pg0 + i);
       }
-      *reinterpret_cast<uint4*>(sQ + sw_off(r, c, RP * 128)) = v;
+      __syncwarp();
+    } else {
+      // the packed query rows (r = qi * G + gg) as the K-major A operand: per 64-column block, RP rows x 128 B
+      // swizzled; the score lanes wait for q_ready
+      for (int idx = threadIdx.x - 32; idx < RP * (D / 8); idx += C::kThreads - 32) {
+        const int r = idx / (D / 8);
+        const int c = idx - r * (D / 8);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < p.R) {
+          const int qi = r / p.G;
+          v = *reinterpret_cast<const uint4*>(p.q + static_cast<int64_t>(b * p.Q + qi) * p.sq_t +
+                                              static_cast<int64_t>(hq0 + r - qi * p.G) * p.sq_h + c * 8);
+        }
+        *reinterpret_cast<uint4*>(sQ + sw_off(r, c, RP * 128)) = v;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the query tile is read by the tensor cores
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the query tile is read by the tensor cores
-    __syncthreads();
 
     if (warp == 0) {
       // ---------------------------------------------------------------------------------------- TMA producer
@@ -765,8 +775,10 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-    } else if (warp == 1) {
-      // ---------------------------------------------------------------------------------------- MMA issuer
+    } else if (warp == 1 || warp == 6) {
+      // ---------------------------------------------------------------------------------------- MMA issuers
+      // warp 1 lane 0 issues the score products, warp 6 lane 0 the value products: neither waits for the other's
+      // inputs (scores need K pieces and a free S buffer, values need P and V pieces)
       if (lane == 0) {
         constexpr uint32_t idesc_s = idesc_bf16(C::kRows, C::kTile, false, false);
         constexpr uint32_t idesc_o = idesc_bf16(C::kRows, D, false, true);
@@ -785,6 +797,10 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           return true;
         };
+        if (warp == 1 && !sa_wait(q_ready, 0, sAbort)) {
+          sa_abort(p, sAbort);
+          ok = false;
+        }
         auto issue_s = [&](int i) -> bool {
           const int sb = i & 1;
           if (i >= 2 && !sa_wait(&s_free[sb], ((i >> 1) - 1) & 1, sAbort)) {
@@ -830,12 +846,12 @@ __global__ void __launch_bounds__(192, 1)
           mma_commit(&pv_done[sb]);
           return true;
         };
-        if (n_tiles > 0) ok = issue_s(0);
-        for (int i = 0; i < n_tiles && ok; ++i) {
-          if (i + 1 < n_tiles) ok = issue_s(i + 1);
-          if (ok) ok = issue_pv(i);
+        if (warp == 1) {
+          for (int i = 0; i < n_tiles && ok; ++i) ok = issue_s(i);
+        } else {
+          for (int i = 0; i < n_tiles && ok; ++i) ok = issue_pv(i);
         }
-        // every issued MMA has completed before the roles finish (and tensor memory is freed)
+        // every issued MMA of both lanes has completed before the roles finish (and tensor memory is freed)
         mma_commit(drain);
         const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kSaWaitNs) {
