@@ -483,31 +483,66 @@ __global__ void __launch_bounds__(SaGeo<D, MT>::kThreads, 1)
   }
 }
 
+// Loads issued in program order (volatile asm: the compiler neither sinks them below a branch nor drops them), plain
+// weak global loads like the compiler's own.
+__device__ __forceinline__ int ld_issue_s32(const int* ptr) {
+  int v;
+  asm volatile("ld.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr));
+  return v;
+}
+__device__ __forceinline__ float ld_issue_f32(const float* ptr) {
+  float v;
+  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(ptr));
+  return v;
+}
+__device__ __forceinline__ float4 ld_issue_f32x4(const float4* ptr) {
+  float4 v;
+  asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(ptr));
+  return v;
+}
+
 // Merge of the splits: one CTA of 256 threads per output row (request, KV head, packed row r); thread (group sg,
-// column quad c) sums the splits s = sg, sg + NG, ... of its four columns, so that every partial load of the row is
-// issued at once.  out = sum_s 2^(lse_s - m) o_s / sum_s 2^(lse_s - m), m = max_s lse_s (zeros when every split is
-// empty).  Rows of requests with a single split were written by spec_attn_kernel.
+// column quad c) sums the splits s = sg, sg + NG, ... of its four columns.  The request's length, every split's
+// log-sum-exp and the first kMergeSpec splits of each thread are loaded at once, before the split count is known (the
+// slots of every possible split lie in the workspace; those at or past the count are never used), so the merge costs
+// one memory round trip after the dependency wait instead of three.  out = sum_s 2^(lse_s - m) o_s /
+// sum_s 2^(lse_s - m), m = max_s lse_s (zeros when every split is empty).  Rows of requests with a single split were
+// written by the attention kernel.
+constexpr int kMergeSpec = 12;
 template <int D>
 __global__ void __launch_bounds__(256) spec_attn_merge_kernel(const SaParams p) {
   constexpr int NQ = D / 4;    // float4 columns per row
   constexpr int NG = 256 / NQ; // split groups
+  static_assert(kSaMaxSplits <= 256, "one log-sum-exp per thread");
   __shared__ float sW[kSaMaxSplits];
   __shared__ float sRed[8];
   __shared__ float4 sAcc[NG][NQ];
   pdl_launch_dependents();  // the next kernel's prologue may overlap this one; it reads nothing written here before
                             // its own griddepcontrol.wait
-  pdl_wait();  // the partial outputs of spec_attn_kernel
+  pdl_wait();  // the partial outputs of the attention kernel
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int r = row % p.R;
   const int bh = row / p.R;
   const int b = bh / p.HKV;
   const int hkv = bh - b * p.HKV;
-  int chunk, n_split;
-  sa_split(__ldg(p.seq_lens + b), p.max_splits, chunk, n_split);
-  if (n_split == 1) return;
+  const int sg = tid / NQ;
+  const int c = tid - sg * NQ;
   const int64_t row0 = static_cast<int64_t>(bh) * p.max_splits * p.R + r;  // split s at row0 + s * R
-  const float l = tid < n_split ? p.lse_part[row0 + static_cast<int64_t>(tid) * p.R] : -INFINITY;
+  const float4* src = reinterpret_cast<const float4*>(p.o_part + row0 * D) + c;
+  const int seq_len = ld_issue_s32(p.seq_lens + b);
+  const float l_any = tid < p.max_splits ? ld_issue_f32(p.lse_part + row0 + static_cast<int64_t>(tid) * p.R) : 0.f;
+  float4 v[kMergeSpec];
+#pragma unroll
+  for (int k = 0; k < kMergeSpec; ++k) {
+    const int s = sg + k * NG;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s < p.max_splits) v[k] = ld_issue_f32x4(src + static_cast<int64_t>(s) * p.R * NQ);
+  }
+  int chunk, n_split;
+  sa_split(seq_len, p.max_splits, chunk, n_split);
+  if (n_split == 1) return;
+  const float l = tid < n_split ? l_any : -INFINITY;
   float m = l;
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
@@ -528,18 +563,26 @@ __global__ void __launch_bounds__(256) spec_attn_merge_kernel(const SaParams p) 
   den = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) den += sRed[i];
-  const int sg = tid / NQ;
-  const int c = tid - sg * NQ;
-  const float4* src = reinterpret_cast<const float4*>(p.o_part + row0 * D) + c;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int s = sg; s < n_split; s += NG) {
+#pragma unroll
+  for (int k = 0; k < kMergeSpec; ++k) {
+    const int s = sg + k * NG;
+    if (s < n_split) {  // slots past the count may hold anything, NaN included: never touched
+      const float ws = sW[s];
+      acc.x = fmaf(ws, v[k].x, acc.x);
+      acc.y = fmaf(ws, v[k].y, acc.y);
+      acc.z = fmaf(ws, v[k].z, acc.z);
+      acc.w = fmaf(ws, v[k].w, acc.w);
+    }
+  }
+#pragma unroll 4
+  for (int s = sg + kMergeSpec * NG; s < n_split; s += NG) {
     const float ws = sW[s];
-    const float4 v = src[static_cast<int64_t>(s) * p.R * NQ];
-    acc.x = fmaf(ws, v.x, acc.x);
-    acc.y = fmaf(ws, v.y, acc.y);
-    acc.z = fmaf(ws, v.z, acc.z);
-    acc.w = fmaf(ws, v.w, acc.w);
+    const float4 u = src[static_cast<int64_t>(s) * p.R * NQ];
+    acc.x = fmaf(ws, u.x, acc.x);
+    acc.y = fmaf(ws, u.y, acc.y);
+    acc.z = fmaf(ws, u.z, acc.z);
+    acc.w = fmaf(ws, u.w, acc.w);
   }
   sAcc[sg][c] = acc;
   __syncthreads();
