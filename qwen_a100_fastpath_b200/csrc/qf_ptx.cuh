@@ -303,6 +303,28 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] x B[smem desc]^T, bf16 operands, fp32 accumulators (kind::f16; one thread issues).  A sits in
+// tensor memory K-major: row m on lane m, k along the columns, two 16-bit elements per 32-bit column (the lower k in
+// the low half), so a K = 16 step spans 8 columns.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 8 consecutive 32-bit columns of the warp's 32 tensor-memory lanes: thread t gets lane (lane base + t).
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // Instruction descriptor of tcgen05.mma kind::f16 with bf16 A and B and an fp32 accumulator, M x N; a_mn / b_mn
 // select the MN-major (transposed) operand layout instead of K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn, bool b_mn) {
@@ -318,8 +340,9 @@ __device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t smem_addr, uint3
          (static_cast<uint64_t>(sbo >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Stores 32 consecutive 32-bit columns of the warp's 32 tensor-memory lanes (thread t writes lane base + t).
-__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+// Stores 32 consecutive 32-bit columns of the warp's 32 tensor-memory lanes (thread t writes lane base + t), then
+// waits for this thread's stores to complete unless `wait` is false.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32], bool wait = true) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
       "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
@@ -328,7 +351,7 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  if (wait) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // fp32 -> int8 with round-to-nearest-even and saturation to [-128, 127]; NaN -> 0.

@@ -33,6 +33,17 @@
 //   weight conversion is exact in both paths; the fp16 activation is exact except below fp16's normal range
 //   (|x| < 2^-14), where it rounds to an fp16 subnormal (absolute error <= 2^-25 per activation, far below the
 //   fp32 accumulation noise).  QF_F16_PATH=0 (under QF_TEST_OVERRIDES=1) keeps every product exact.
+// * Tensor-core consumers (TC instances, opt-in: 128-row tiles of 256-byte stages, 9..16 tokens): the eight consumer
+//   warps convert their rows to exact bf16 and store them into tensor memory (warp w: lanes 32 (w % 4) .., weight
+//   box w / 4 of the stage), and one thread of an eleventh warp issues tcgen05.mma kind::f16 with that A operand,
+//   the activation boxes as the 16-column B operand straight from shared memory and the tile's fp32 sums in tensor
+//   memory (two A buffers and two accumulators, so conversion, MMA and the tile-end read-out overlap).  At a tile
+//   end the consumers copy the sums into the shared-memory layout the epilogue warp reads.  Every product is exact
+//   (bf16 x int8-valued bf16).  Measured on B200 it is slower than the mma.sync consumers at every shape (gate_up at
+//   16 tokens 47.7 against 34.5 us): an M = 128, N = 16, K = 16 MMA costs about as long as a wide one, so the 16 MMAs
+//   of a 32 KiB stage take longer than HBM needs to deliver the stage (removing the MMAs, not the tensor-memory
+//   stores, brings it back to 33.8 us; two or four independent accumulators change nothing).  Kept for measurement
+//   and tests (QF_TC=1); the mma.sync consumers are the default.
 // * Epilogue: fp32 accumulator * scale, one rounding to bf16 (or fp32 export), optional bias as the reference's
 //   second bf16 rounding (`y + bias`); a dedicated warp finishes each tile while the consumers stream the next,
 //   and the consumers finish a CTA's last tile together.  The head additionally reduces each tile's bf16 logits
@@ -64,6 +75,10 @@ constexpr int kConsumerWarps = 8;
 constexpr int kProducerWarp = 8;            // TMA issue (one lane)
 constexpr int kEpilogueWarp = 9;            // tile epilogues and stream-K reductions
 constexpr int kThreads = 10 * 32;
+constexpr int kMmaWarp = 10;                // TC instances: tcgen05.mma issue (one lane)
+constexpr int kTcThreads = 11 * 32;
+constexpr uint32_t kTcCols = 512;           // TC: A buffers 2 x 128 columns, accumulators 2 x 16
+constexpr uint32_t kTcColD = 256;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kMaxBN = 128;
 constexpr int kMaxGrid = 256;
@@ -120,12 +135,13 @@ template <int BN, int NT, int KS, bool NORM = false> struct Geo {
   static constexpr int kOffRed = kOffX + kStages * kXStageBytes;
   static constexpr int kOffStat = kOffRed + kRedBytes;
   static constexpr int kOffOut = kOffStat + kStatBytes;
-  static constexpr int kOffBar = kOffOut + kOutBytes;         // full[S], empty[S]
-  static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;  // abort, last
+  static constexpr int kOffBar = kOffOut + kOutBytes;         // full[S], empty[S], then 8 for the TC instances
+  static constexpr int kOffFlag = kOffBar + 2 * kStages * 8 + 64;  // abort, last, coop, tensor-memory address
   static constexpr int kOffNorm = kOffFlag + 64;               // fused RMSNorm data
   static constexpr int kSmemBytes = kOffNorm + kNormBytes + 1024;  // + alignment slack
   static_assert(BPW >= 1 && B * NMW == 4 * BPW && 4 % NMW == 0, "the four warp pairs cover the stage's boxes evenly");
   static_assert(kStages >= 3, "pipeline too shallow");
+  static_assert(2 * kStages * 8 + 64 <= 2 * 16 * 8, "barriers within their reservation");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -941,10 +957,12 @@ __device__ __forceinline__ void fold_tile(const Params& p, int lane, float4* sTi
   __syncwarp();
 }
 
-template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU, bool NORM>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU, bool NORM, bool TC>
+__global__ void __launch_bounds__(TC ? kTcThreads : kThreads, 1)
     w8a16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_r, const Params p) {
+  static_assert(!TC || (BN == 128 && KS == 256 && NT == 2 && !NORM),
+                "tensor-core consumers: 128-row tiles, 256-byte stages, two token tiles, no fused RMSNorm");
   static_assert(!(HEAD && AR), "the head is vocab-parallel: no all-reduce");
   static_assert(!(SILU && (HEAD || AR)), "the fused gate is for the column-parallel gate_up only");
   static_assert(!(NORM && (HEAD || AR)), "the fused RMSNorm is for the column-parallel qkv and gate_up");
@@ -966,6 +984,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::kOffFlag);
   volatile int* sLast = sAbort + 1;
   volatile int* sCoop = sAbort + 2;  // last tile: 0 epilogue warp finishes it, 1 consumers, 2 consumers + peers' sums
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + C::kOffFlag + 12);  // TC: tensor-memory base address
+  // TC: a_full[2] (consumers -> MMA: A buffer stored), a_free[2] (MMA commit: A buffer read), d_full[2] (MMA commit:
+  // the tile's sums are complete), d_free[2] (consumers -> MMA: sums read out)
+  uint64_t* a_full = full_bar + 2 * S;
+  uint64_t* a_free = a_full + 2;
+  uint64_t* d_full = a_full + 4;
+  uint64_t* d_free = a_full + 6;
   // fused RMSNorm: the consumer warps' per-token sums of z^2 of the tile being handed off, [8 warps][16 tokens]
   float* sSsq = reinterpret_cast<float*>(smem + C::kOffNorm + (kNormMaxK + 1024) * 2);
   // the CTA's last tile is finished by the consumer warps (plain GEMM instances with bf16 output)
@@ -981,14 +1006,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (NORM && p.res) prefetch_tensormap(&tmap_r);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kConsumerWarps);  // one arrival per consumer warp
+      mbar_init(&empty_bar[s], TC ? 1 : kConsumerWarps);  // one arrival per consumer warp (TC: the MMA commit)
+    }
+    if constexpr (TC) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&a_full[b], kConsumerWarps);
+        mbar_init(&a_free[b], 1);
+        mbar_init(&d_full[b], 1);
+        mbar_init(&d_free[b], kConsumerWarps);
+      }
     }
     *sAbort = 0;
     *sLast = 0;
     *sCoop = 0;
     fence_mbar_init();
   }
+  if (TC && warp == kMmaWarp) tmem_alloc(sTmem, kTcCols);
+  if constexpr (TC) tc_fence_before();
   __syncthreads();
+  if constexpr (TC) tc_fence_after();
   pdl_launch_dependents();
 
   StageIter it;
@@ -997,6 +1033,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first and last tile of this CTA's stream-K range (partial unless the range covers them whole)
   const int sk_t0 = it.n_sk > 0 ? it.sk_begin / p.kiters : -1;
   const int sk_t1 = it.n_sk > 0 ? (it.sk_end - 1) / p.kiters : -1;
+
+  if constexpr (TC) {
+    if (warp == kMmaWarp) {
+      // ---------------------------------------------------------------- MMA issue (one lane), TC instances
+      // Per stage: wait for the consumers' bf16 rows of both weight boxes (A buffer i % 2), then 16 MMAs of K = 16:
+      // D [128 rows x 16 tokens] (+)= A [128 x 16] x X^T, X the stage's activation boxes read in place (K-major,
+      // 128-byte swizzle, 8-token groups 1 KiB apart; k step j at +32 bytes in box j / 4).  Commits release the A
+      // buffer, the stage's shared memory (weights converted, activations read) and, at a tile end, the sums.
+      const uint32_t tmem = *sTmem;
+      if (lane == 0) {
+        constexpr uint32_t idesc = idesc_bf16(128, 16, false, false);
+        StageIter mi = it;
+        bool tile_start = true;
+        int tcn = 0;  // tiles started before the current one
+        for (int i = 0; i < n_iter; ++i) {
+          const int s = i % S;
+          const int buf = i & 1;
+          const bool tile_end = (mi.kk == p.kiters - 1) || (mi.sk && i == mi.n_sk - 1);
+          mi.next(p);
+          const int d = tcn & 1;
+          bool ok = true;
+          if (tile_start && tcn >= 2) ok = mbar_wait_bounded(&d_free[d], ((tcn >> 1) - 1) & 1, sAbort);
+          ok = ok && mbar_wait_bounded(&a_full[buf], (i >> 1) & 1, sAbort);
+          if (!ok && !*sAbort) {
+            record_error(p.ws, QF_ERR_TIMEOUT);
+            *sAbort = 1;
+          }
+          tc_fence_after();
+          if (!*sAbort) {
+            const uint32_t xs = smem_u32(sX + s * C::kXStageBytes);
+#pragma unroll
+            for (int j = 0; j < KS / 16; ++j)
+              mma_bf16_ts(tmem + kTcColD + 16 * d, tmem + 128 * buf + 8 * j,
+                          smem_desc_k128_sw128(xs + (j >> 2) * C::kXBoxBytes + (j & 3) * 32), idesc,
+                          (tile_start && j == 0) ? 0u : 1u);
+          }
+          // commits arrive even after an abort (nothing pending), so every role passes its waits
+          mma_commit(&a_free[buf]);
+          mma_commit(&empty_bar[s]);
+          if (tile_end) {
+            mma_commit(&d_full[d]);
+            ++tcn;
+          }
+          tile_start = tile_end;
+        }
+        // the consumers' read-out of the last tile precedes the release of tensor memory (bounded, abort or not)
+        if (tcn > 0) {
+          const uint32_t par = static_cast<uint32_t>(((tcn - 1) >> 1) & 1);
+          const uint64_t t0 = global_timer_ns();
+          while (!mbar_try_wait(&d_free[(tcn - 1) & 1], par) && global_timer_ns() - t0 < kWaitBudgetNs) {
+          }
+        }
+      }
+      __syncwarp();
+      tc_fence_after();
+      tmem_dealloc(tmem, kTcCols);
+      return;
+    }
+  }
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ producer (one lane)
@@ -1324,6 +1419,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       *reinterpret_cast<uint4*>(sX + box * C::kXBoxBytes + (p.M + rem / 8) * 128 + (rem % 8) * 16) =
           make_uint4(0u, 0u, 0u, 0u);
     }
+    if constexpr (TC) {
+      // the tile sums go to one holder slot per m-tile; the other slots the epilogue adds stay zero
+      for (int idx = threadIdx.x; idx < C::kRedBytes / 16; idx += kConsumerThreads)
+        reinterpret_cast<uint4*>(sRed)[idx] = make_uint4(0u, 0u, 0u, 0u);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeroed token rows feed the tensor cores
+    }
     named_bar_sync(kBarConsumers, kConsumerThreads);
   }
   pdl_wait();  // activations, outputs and workspace belong to the previous kernel until it completes
@@ -1352,6 +1453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t x_u1 = static_cast<uint32_t>(((2 * (c & 3) + 1) ^ g) << 4);
   const int ctid = threadIdx.x;  // 0..255 among consumers
   const bool use_f16 = p.f16_path != 0;
+  const uint32_t tmem = TC ? *sTmem : 0u;
+  const uint32_t tc_lanes = static_cast<uint32_t>(32 * (warp & 3)) << 16;  // TC: this warp's tensor-memory lanes
   int tcount = 0;
   // scales and bias of the CTA's last tile (its last whole tile, else the last tile of its stream-K share), which the
   // consumers may finish themselves
@@ -1381,6 +1484,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
       *sAbort = 1;
     }
+    if constexpr (TC) {
+      // row 32 (warp % 4) + lane of weight box warp / 4 as exact bf16 into A buffer i % 2 (columns 64 (warp / 4) ..,
+      // k pairs per column), once the MMAs of stage i - 2 have read that buffer
+      const int buf = i & 1;
+      if (i >= 2 && !mbar_wait_bounded(&a_free[buf], ((i >> 1) - 1) & 1, sAbort)) {
+        if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
+        *sAbort = 1;
+      }
+      tc_fence_after();
+      const int row = 32 * (warp & 3) + lane;
+      const uint32_t wrow = sW_u32 + s * C::kWBytes + (warp >> 2) * C::kWBoxBytes + row * 128;
+      uint32_t a0[32], a1[32];
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint4 v = lds128(wrow + ((cc ^ (row & 7)) << 4));
+        uint32_t* dst = cc < 4 ? a0 + 8 * cc : a1 + 8 * (cc - 4);
+        dequant_i8x4_bf16(v.x, dst[0], dst[1]);
+        dequant_i8x4_bf16(v.y, dst[2], dst[3]);
+        dequant_i8x4_bf16(v.z, dst[4], dst[5]);
+        dequant_i8x4_bf16(v.w, dst[6], dst[7]);
+      }
+      const uint32_t ta = tmem + tc_lanes + 128 * buf + 64 * (warp >> 2);
+      tmem_st_32x32b_x32(ta, a0);
+      tmem_st_32x32b_x32(ta + 32, a1);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[buf]);
+    } else {
 #pragma unroll
     for (int jb = 0; jb < C::BPW; ++jb) {
       const int db = jb * (4 / NMW);  // box offset from b0
@@ -1452,12 +1583,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < MW; ++j) mma_chunk<NT, false>(acc[j], ra[j], rb[j], xa, xb);
       }
     }
+    }
 
     // ------------------------------------------------------------ tile end: hand the sums to the epilogue warp
     const bool tile_end = (it.kk == p.kiters - 1) || (it.sk && i == it.n_sk - 1);
     const int cur_tile = it.tile;
     it.next(p);
     if (!tile_end) continue;
+    if constexpr (TC) {
+      // the tile's sums: tokens 8 (warp / 4) .. + 7 of row 32 (warp % 4) + lane, from accumulator tcount % 2
+      const int d = tcount & 1;
+      if (!mbar_wait_bounded(&d_full[d], (tcount >> 1) & 1, sAbort)) {
+        if (!*sAbort) record_error(p.ws, QF_ERR_TIMEOUT);
+        *sAbort = 1;
+      }
+      tc_fence_after();
+      uint32_t r8[8];
+      tmem_ld_32x32b_x8(tmem + tc_lanes + kTcColD + 16 * d + 8 * (warp >> 2), r8);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&d_free[d]);
+      if (tcount > 0) named_bar_sync(kBarFree, kConsumerThreads + 32);  // the previous tile's sums have been read
+      // into the slot of the first warp holding the m-tile in the mma.sync layout: lane (g, t) holds rows g, g + 8 and
+      // tokens 8 nt + 2 t, + 1 as acc[nt][0..3]
+      const int row = 32 * (warp & 3) + lane;
+      const int mt = row >> 4;
+      float* slot = sRed + ((2 * (mt / MW) * MW + mt % MW) * 32 + 4 * (row & 7)) * 4 * NT + 4 * (warp >> 2) +
+                    2 * ((row >> 3) & 1);
+#pragma unroll
+      for (int tt = 0; tt < 4; ++tt)
+        *reinterpret_cast<float2*>(slot + tt * 4 * NT) =
+            make_float2(__uint_as_float(r8[2 * tt]), __uint_as_float(r8[2 * tt + 1]));
+    } else {
     if (tcount > 0) named_bar_sync(kBarFree, kConsumerThreads + 32);  // the previous tile's sums have been read
     {
       float* mine = sRed + (warp * MW * 32 + lane) * 4 * NT;
@@ -1481,6 +1638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (NT == 1 && lane < 8) sSsq[warp * 16 + 8 + lane] = 0.f;
       }
+    }
     }
     if (kCoopLast && !p.y_f32 && i == n_iter - 1) {  // the CTA's last tile: finished here unless the epilogue
       named_bar_sync(kBarReady, kConsumerThreads + 32);  // warp keeps it (stream-K contribution)
@@ -1654,6 +1812,16 @@ int f16_path() {
   return v;
 }
 
+// Tensor-core consumers for the 128 x 256 tiles at 9..16 tokens (QF_TC=1 under QF_TEST_OVERRIDES=1); off by default,
+// the measured choice (the mma.sync consumers are faster at every shape).
+int tc_mode() {
+  static const int v = [] {
+    const char* e = test_env("QF_TC");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
               uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
   cuuint64_t dims[2] = {inner, rows};
@@ -1707,11 +1875,11 @@ void pick_tiles(int N, int K, int sms, int* bn, int* ks, int* dp_grid) {
   }
 }
 
-template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU, bool NORM>
+template <int BN, int NT, int KS, int HEAD, bool AR, bool SILU, bool NORM, bool TC = false>
 int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, DeviceInfo* dinfo, int dev,
            unsigned flags, cudaStream_t stream) {
   using C = Geo<BN, NT, KS, NORM>;
-  auto kern = w8a16_kernel<BN, NT, KS, HEAD, AR, SILU, NORM>;
+  auto kern = w8a16_kernel<BN, NT, KS, HEAD, AR, SILU, NORM, TC>;
   static bool smem_attr_set[64] = {};
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -1775,7 +1943,7 @@ int launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& p, 
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.G);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(TC ? kTcThreads : kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1795,6 +1963,9 @@ int launch_nt(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, Params& 
   // the fused RMSNorm also stages the residual: with two token tiles the 512- and 1024-byte stages would leave fewer
   // than three ring stages, so those tile heights run with half the k bytes per stage
   constexpr int KS2 = (NORM && KS >= 512 && BN * KS >= 32768) ? KS / 2 : KS;
+  if constexpr (BN == 128 && KS2 == 256 && !NORM) {
+    if (tc_mode() == 1) return launch<BN, 2, KS2, HEAD, AR, SILU, NORM, true>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
+  }
   return launch<BN, 2, KS2, HEAD, AR, SILU, NORM>(x, ldx, w, ldw, p, dinfo, dev, flags, st);
 }
 
