@@ -199,6 +199,7 @@ class Step:
         self.torch = torch
         self.M, self.rank, self.world, self.dev, self.pdl = M, rank, world, dev, pdl
         self.ar = None
+        self.ar_off = False  # tensor-parallel breakdown only: row-parallel shards without their all-reduce
         self.fused = world > 1 and allreduce == "fused"
         if world > 1 and allreduce in ("nvlink", "fused"):
             from qwen_a100_fastpath_b200.tp import NVLinkAllReduce
@@ -253,7 +254,7 @@ class Step:
         for ws in self.layers:
             for name, _, _, style in LAYER:
                 w, s = ws[name]
-                fused_row = self.fused and style == "row"
+                fused_row = self.fused and style == "row" and not self.ar_off
                 if fused_row:  # row-parallel GEMM with the all-reduce in its epilogue
                     y = w8a16_mm_allreduce(self.x[name], w, s, self.ar, out=None if linear else self.y[name],
                                            pdl=self.pdl)
@@ -264,7 +265,7 @@ class Step:
                 if events is not None:
                     events[e].record()
                     e += 1
-                if style == "row" and self.world > 1 and not fused_row:
+                if style == "row" and self.world > 1 and not fused_row and not self.ar_off:
                     if self.ar is not None:
                         self.ar(y, pdl=self.pdl)
                     else:
@@ -376,7 +377,7 @@ def run_ours(args, rank: int, world: int, local: int):
     #     the head: the decoder-GEMM phase / its launch count is the kernel's average launch duration in the
     #     running workload (world == 1; with TP the phase also holds the all-reduces)
     phase = None
-    if world == 1:
+    if True:  # with TP the decoder-GEMM phase also holds the all-reduces (reported apart below)
         try:
             pev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
             gp = torch.cuda.CUDAGraph()
@@ -424,12 +425,12 @@ def run_ours(args, rank: int, world: int, local: int):
         del g2
         n_gemm = st.launches_per_step - 1
         iso_launch_ms = statistics.median(gemm_ms) / n_gemm
-        per_launch_ms = phase[0] / n_gemm if phase else iso_launch_ms
+        per_launch_ms = phase[0] / n_gemm if (phase and world == 1) else iso_launch_ms
         gemm_bytes = sum(st.gemm_bytes(nm) for nm, *_ in LAYER) * args.layers / n_gemm
         peak, peak_src = peak_hbm()
         achieved = gemm_bytes / (per_launch_ms * 1e-3) / 1e9
         traffic, tsrc = traffic_from_profiles()
-        head_launch_ms = phase[1] if phase else statistics.median(head_ms)
+        head_launch_ms = phase[1] if (phase and world == 1) else statistics.median(head_ms)
         head_bytes = alg_bytes(st.head_n, HEAD[2], args.m, head=True)
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -440,7 +441,8 @@ def run_ours(args, rank: int, world: int, local: int):
                                        "launch of the decoder GEMMs of a committed M=5 step capture, not measured "
                                        "by this run" if tsrc else None),
                     "timing": ("decoder-GEMM phase of the step graph (PDL on) between CUDA events at the step start "
-                               "and after the last GEMM, / 256 launches, median over replays" if phase else
+                               "and after the last GEMM, / 256 launches, median over replays" if (phase and world == 1)
+                               else
                                "CUDA events around every launch of a replay of the same step (PDL off), median of 5"),
                     "us_per_launch_isolated": round(iso_launch_ms * 1e3, 3),
                     "head": {"us": round(head_launch_ms * 1e3, 2),
@@ -454,6 +456,42 @@ def run_ours(args, rank: int, world: int, local: int):
             us = statistics.median(vals) * 1e3
             roofline["per_gemm_us"][nm] = {"us_isolated": round(us, 2),
                                            "GBps": round(st.gemm_bytes(nm) / (us * 1e-6) / 1e9, 1)}
+        if world > 1:
+            # where the time goes with TP: the same instrumented replay with the row-parallel shards run as plain
+            # GEMMs (no all-reduce); every rank runs it, so the collectives stay in step
+            st.ar_off = True
+            g3 = torch.cuda.CUDAGraph()
+            st.pdl = False
+            with torch.cuda.graph(g3, stream=stream):
+                st.run(events=events)
+            st.pdl = saved_pdl
+            st.ar_off = False
+            with torch.cuda.stream(stream):
+                g3.replay()
+            torch.cuda.synchronize()
+            plain = {nm: [] for nm, *_r in LAYER}
+            for _ in range(reps):
+                with torch.cuda.stream(stream):
+                    g3.replay()
+                torch.cuda.synchronize()
+                d3 = [events[i].elapsed_time(events[i + 1]) for i in range(n_ev - 1)]
+                for j, (nm, *_r) in enumerate(LAYER):
+                    plain[nm].append(statistics.median(d3[j:n_gemm:len(LAYER)]))
+            del g3
+            tpb = {"decoder_phase_us_per_layer": round(phase[0] * 1e3 / args.layers, 2) if phase else None,
+                   "row_parallel_us": {}, "timing": "CUDA events around every launch (PDL off), median"}
+            extra_ms = 0.0
+            for nm, _n, _k, style in LAYER:
+                if style != "row":
+                    continue
+                with_ar = roofline["per_gemm_us"][nm]["us_isolated"]
+                gemm_only = statistics.median(plain[nm]) * 1e3
+                tpb["row_parallel_us"][nm] = {"with_allreduce": with_ar, "gemm_only": round(gemm_only, 2),
+                                              "allreduce": round(with_ar - gemm_only, 2)}
+                extra_ms += (with_ar - gemm_only) * 1e-3 * args.layers
+            tpb["allreduce_ms_per_step"] = round(extra_ms, 3)
+            tpb["allreduce_share_of_step"] = round(extra_ms / ms, 4)
+            roofline["tp"] = tpb
     except Exception as e:  # noqa: BLE001
         roofline = {"error": f"instrumented replay failed: {e!r}"}
 
